@@ -1,0 +1,79 @@
+/*
+ * qflash_b200 -- C ABI of the B200 (sm_100a) integer-only attention forward.
+ *
+ * The functions below are what a host binding (Python ctypes, a C/C++
+ * caller, a cgo/JNI stub) calls.  Buffers are plain device pointers owned by
+ * the caller; the library allocates no device memory.  Calls are asynchronous
+ * on the given CUDA stream and return a status code (0 = launched).
+ *
+ * Reference: EfficientCompLab/qflash, qflash/kernel.py.
+ */
+#ifndef QFLASH_B200_H_
+#define QFLASH_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define QFLASH_OK 0
+#define QFLASH_ERR_ARG (-1)         /* bad shape, head dim, null pointer, parameter */
+#define QFLASH_ERR_ALIGN (-2)       /* pointer or stride alignment the TMA path cannot take */
+#define QFLASH_ERR_TMA (-3)         /* tensor-map encoding failed */
+#define QFLASH_ERR_LAUNCH (-4)      /* kernel launch failed */
+#define QFLASH_ERR_DEVICE (-5)      /* no sm_100 device / driver entry point missing */
+#define QFLASH_ERR_UNSUPPORTED (-6) /* combination not implemented */
+
+/* flags: the reference's QFLASH_* arithmetic switches (qflash/kernel.py:30-36)
+ * and the final-division rounding. 0 = the reference defaults. */
+#define QFLASH_FLAG_EXP_IDIV 1u  /* QFLASH_EXP_USE_SHIFT=0: exp2_i32_idiv (kernel.py:47-51) */
+#define QFLASH_FLAG_L_IDIV 2u    /* QFLASH_L_USE_SHIFT=0: scale_release_idiv for l (kernel.py:72-74) */
+#define QFLASH_FLAG_ACC_IDIV 4u  /* QFLASH_ACC_USE_SHIFT=0: scale_release_idiv for acc */
+#define QFLASH_FLAG_DIV_FULL 8u  /* final acc/l with the approximate fp32 divide (div.full.f32) that the
+                                    reference's compiled GPU kernel uses; default is IEEE round-to-nearest */
+
+/*
+ * Integer attention forward: O = int8(acc / l) of the chunked integer online
+ * softmax over int8 Q, K, V.
+ *
+ * Replaces the Triton launches qflash_kernel[grid](...) (qflash/kernel.py:319-326)
+ * and qflash_masked_kernel[grid](...) (qflash/kernel.py:339-346); the
+ * arguments are those launches' arguments:
+ *   q, k, v, o      int8 [Z, H, N, D]; strides in elements, innermost (D) stride must be 1
+ *   bias            int32 additive bias broadcastable to [Z, H, N, N] (NULL = unmasked
+ *                   kernel); bias_strides in elements, 0 for a broadcast dimension, and
+ *                   its row stride must be a multiple of 4 elements (16 bytes)
+ *   D               32, 64, 128 or 256
+ *   sm_rscale, exp_M, req_M, l_M, acc_M   the host-derived fixed-point constants
+ *                   (kernel.py:302-307)
+ *   l_shift, acc_shift   QFLASH_L_SHIFT / QFLASH_ACC_SHIFT (1..62)
+ *   flags           QFLASH_FLAG_*
+ *   stream          cudaStream_t (NULL = legacy default stream)
+ * Pointers and the q/k/v/bias strides of the three outer dimensions must be 16-byte aligned.
+ */
+int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                  const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                  const int64_t o_strides[4], const int64_t bias_strides[4], int Z, int H, int N, int D,
+                  int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
+                  int32_t acc_shift, uint32_t flags, void* stream);
+
+/* Reads and clears the device-side error word the kernels set when a bounded
+ * wait gives up (0 = none).  Synchronises the stream. */
+int qflash_device_error(void* stream, uint32_t* out);
+
+/* Number of kernel launches issued by this library since load (for accounting). */
+uint64_t qflash_launch_count(void);
+
+/* Library version string. */
+const char* qflash_version(void);
+
+/* Human-readable text of the last error on the calling thread. */
+const char* qflash_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QFLASH_B200_H_ */

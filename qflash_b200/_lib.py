@@ -1,0 +1,92 @@
+"""ctypes binding of the C ABI declared in include/qflash_b200.h.
+
+This is the binding a maintainer of the reference would add: plain pointers,
+sizes and strides, no torch types crossing the boundary.  The library must be
+present (``python -m qflash_b200.build``); there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libqflash_b200.so"
+
+FLAG_EXP_IDIV = 1
+FLAG_L_IDIV = 2
+FLAG_ACC_IDIV = 4
+FLAG_DIV_FULL = 8
+
+ERRORS = {-1: "QFLASH_ERR_ARG", -2: "QFLASH_ERR_ALIGN", -3: "QFLASH_ERR_TMA", -4: "QFLASH_ERR_LAUNCH",
+          -5: "QFLASH_ERR_DEVICE", -6: "QFLASH_ERR_UNSUPPORTED"}
+
+# name -> (restype, argtypes); every symbol the header declares
+_I64x4 = ctypes.POINTER(ctypes.c_int64)
+SIGNATURES = {
+    "qflash_i8_fwd": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        _I64x4, _I64x4, _I64x4, _I64x4, _I64x4,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p]),
+    "qflash_device_error": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "qflash_launch_count": (ctypes.c_uint64, []),
+    "qflash_version": (ctypes.c_char_p, []),
+    "qflash_last_error": (ctypes.c_char_p, []),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class QFlashError(RuntimeError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise if it is missing (no CPU path exists)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise QFlashError(f"{LIB_PATH} is missing: build it with `python -m qflash_b200.build`")
+                lib = ctypes.CDLL(str(LIB_PATH))
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(lib, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = lib
+    return _lib
+
+
+def _strides(t) -> ctypes.Array:
+    return (ctypes.c_int64 * 4)(*[int(s) for s in t.stride()])
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        msg = load().qflash_last_error().decode(errors="replace")
+        raise QFlashError(f"{what} failed: {ERRORS.get(rc, rc)}: {msg}")
+
+
+def i8_fwd(q, k, v, o, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
+           l_shift, acc_shift, flags, stream) -> None:
+    """Launch the attention kernel on device tensors (no synchronisation)."""
+    lib = load()
+    bs = (ctypes.c_int64 * 4)(*bias_strides) if bias is not None else None
+    rc = lib.qflash_i8_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                           bias.data_ptr() if bias is not None else None,
+                           _strides(q), _strides(k), _strides(v), _strides(o), bs,
+                           Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags, stream)
+    _check(rc, "qflash_i8_fwd")
+
+
+def device_error(stream) -> int:
+    out = ctypes.c_uint32(0)
+    _check(load().qflash_device_error(stream, ctypes.byref(out)), "qflash_device_error")
+    return int(out.value)
+
+
+def launch_count() -> int:
+    return int(load().qflash_launch_count())

@@ -1,0 +1,718 @@
+// qflash_b200: integer-only attention forward for B200 (sm_100a).
+//
+// Computes, bit for bit, the int8 output of QFlash's Triton kernels
+// qflash_kernel (qflash/kernel.py:85-180) and qflash_masked_kernel
+// (qflash/kernel.py:183-272): S = Q K^T in int32, an integer online softmax
+// over 32-key chunks taken in order (the chunk width is part of the
+// arithmetic), P requantised to int8, acc = rescale(acc) + P V in int32,
+// O = int8(int32(fp32(acc) / fp32(l))).
+//
+// Structure of one CTA (192 threads) -- a persistent loop over work items, an
+// item being one 128-query-row tile of one (z, h) head:
+//   warps 0-3  softmax: warp w owns TMEM lanes [32w, 32w+32) = query rows of
+//              the tile; acc lives in registers (one row per thread)
+//   warp 4     TMA producer: Q tile, then K/V chunk stages (and bias chunks)
+//   warp 5     TMEM allocator and tcgen05.mma issuer
+// Per 32-key chunk g (counted over the CTA's whole item sequence):
+//   MMA   S_g = Q K_g^T            -> TMEM S slot (g & 1), 32 columns
+//   soft  read S_g, exp2/requant, write packed int8 P_g into the same slot
+//   MMA   PV_g = P_g (TMEM) V_g    -> TMEM PV slot (g & 1), DV columns
+//   soft  acc = rescale(acc, alpha_g) + PV_g
+// The MMA warp issues S_{g+1} before PV_g, so the tensor core computes the
+// next scores while the softmax warps work on the current chunk.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/qflash_b200.h"
+#include "sm100_ptx.cuh"
+
+namespace qfb {
+
+constexpr int kBM = 128;             // query rows per tile = TMEM lanes
+constexpr int kBN = 32;              // keys per chunk (BLOCK_N of the reference)
+constexpr int kNegInf = -(1 << 20);  // qflash/kernel.py:137
+constexpr int kThreads = 192;
+
+__device__ unsigned int g_err;       // set when a bounded wait gives up
+
+// Error codes written to g_err (bit set per site).
+enum : unsigned { kErrQEmpty = 1, kErrKvEmpty = 2, kErrQFull = 4, kErrKvFull = 8, kErrPFull = 16,
+                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128 };
+
+struct KArgs {
+  int Z, H, N, nch, ntiles, nitems;
+  int bias_hb, bias_zb;      // 1 if the bias has a real H / Z dimension, 0 if broadcast
+  int v_col0;                // first output column handled (head dim 256 runs as two halves)
+  int8_t* o;
+  long long os_z, os_h, os_n;
+  int o_vec16;               // O rows 16-byte aligned
+  int rs, eM, rM;            // sm_rscale, exp_M, req_M
+  long long lM, accM;
+  int ls, as;                // L_SHIFT, ACC_SHIFT
+  unsigned flags;
+  int fast_exp;              // host proved the 6-op exp2 form exact for this call
+};
+
+// ------------------------------------------------------------------ integer primitives
+// Arithmetic right shift with the reference's semantics for any shift amount:
+// PTX shr.s32 clamps amounts above 32 (read as unsigned) to 32 -> sign fill.
+__device__ __forceinline__ int shr_clamp(int a, int b) {
+  int d;
+  asm("shr.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// exp2_i32_shift / exp2_i32_idiv (qflash/kernel.py:40-51), int32 wrap-around.
+__device__ __forceinline__ int exp2_generic(int x, int rs, int eM, bool idiv) {
+  int q;
+  if (!idiv) {
+    q = (int)((unsigned)x * (unsigned)eM) >> 16;
+  } else {
+    q = (int)(0u - (unsigned)x) / rs;
+  }
+  const int r = (int)((unsigned)x + (unsigned)q * (unsigned)rs);
+  const int h = (int)((unsigned)(r >> 1) + (unsigned)rs);
+  return shr_clamp(h, q);
+}
+
+// exp2_i32_shift of x = s - m in 6 integer ops.  With cm1 = -m*exp_M + 2^16
+// and c3 = rs - m:  t1 = x*exp_M + 2^16, q1 = t1 >> 16 = q + 1,
+// r2 = q1*rs + x + rs = r + 2*rs, and r2 >> q1 = ((r >> 1) + rs) >> q.
+// Exact whenever none of those int32 values wraps and q >= 0; the host
+// establishes that (|exp_M| <= 1023, exp_M <= 0, |x| <= 2^21, rs < 2^26).
+__device__ __forceinline__ int exp2_fast(int s, int eM, int cm1, int rs, int c3) {
+  const int t1 = (int)((unsigned)s * (unsigned)eM + (unsigned)cm1);
+  const int q1 = t1 >> 16;
+  const int u = (int)((unsigned)s + (unsigned)c3);
+  const int r2 = (int)((unsigned)q1 * (unsigned)rs + (unsigned)u);
+  return shr_clamp(r2, q1);
+}
+
+// requantize (qflash/kernel.py:62-64): int8((p * req_M + 2^15) >> 16) is byte 2
+// of the wrapped 32-bit value; pack four of them into one word (byte i = key 4c+i).
+__device__ __forceinline__ uint32_t requant_pack4(int e0, int e1, int e2, int e3, int rM) {
+  const uint32_t p0 = (unsigned)e0 * (unsigned)rM + 32768u;
+  const uint32_t p1 = (unsigned)e1 * (unsigned)rM + 32768u;
+  const uint32_t p2 = (unsigned)e2 * (unsigned)rM + 32768u;
+  const uint32_t p3 = (unsigned)e3 * (unsigned)rM + 32768u;
+  const uint32_t t01 = __byte_perm(p0, p1, 0x0062);
+  const uint32_t t23 = __byte_perm(p2, p3, 0x0062);
+  return __byte_perm(t01, t23, 0x5410);
+}
+
+// scale_release_shift (qflash/kernel.py:67-69) with A = alpha * M already
+// formed: int32(((int64)x * A + 2^(S-1)) >> S), all wrap-around.
+__device__ __forceinline__ int rel_shift64(int x, unsigned long long A, int S) {
+  const unsigned long long v = (unsigned long long)(long long)x * A + (1ull << (S - 1));
+  return (int)((long long)v >> S);
+}
+// scale_release_idiv (qflash/kernel.py:72-74): (x * alpha) // rs, int32 product.
+__device__ __forceinline__ int rel_idiv(int x, int alpha, int rs) {
+  return (int)((unsigned)x * (unsigned)alpha) / rs;
+}
+
+// Final division (qflash/kernel.py:176): int32(fp32(acc) / fp32(l)); a NaN or
+// out-of-range quotient becomes INT32_MIN.
+__device__ __forceinline__ int div_to_i32(int acc, int l, bool full) {
+  const float a = __int2float_rn(acc);
+  const float b = __int2float_rn(l);
+  float qf;
+  if (full) {
+    asm("div.full.f32 %0, %1, %2;" : "=f"(qf) : "f"(a), "f"(b));
+  } else {
+    qf = __fdiv_rn(a, b);
+  }
+  return (qf >= -2147483648.0f && qf < 2147483648.0f) ? __float2int_rz(qf) : (int)0x80000000;
+}
+
+// ------------------------------------------------------------------ kernel
+template <int DQK, int DV, bool BIAS>
+struct Cfg {
+  static constexpr int QA = DQK < 128 ? DQK : 128;  // bytes per row of one swizzle atom
+  static constexpr int NQA = DQK / QA;              // atoms along the QK contraction
+  static constexpr int VA = DV;                     // DV <= 128: one atom
+  static constexpr int KVS = BIAS ? 4 : 8;          // K/V chunk stages
+  static constexpr int Q_BYTES = kBM * DQK;
+  static constexpr int K_BYTES = kBN * DQK;
+  static constexpr int V_BYTES = kBN * DV;
+  static constexpr int B_BYTES = BIAS ? kBM * kBN * 4 : 0;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + KVS * K_BYTES;
+  static constexpr int OFF_B = OFF_V + KVS * V_BYTES;
+  static constexpr int OFF_BAR = OFF_B + KVS * B_BYTES;
+  static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2 + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
+  static constexpr int TMEM_COLS = (64 + 2 * DV) <= 128 ? 128 : ((64 + 2 * DV) <= 256 ? 256 : 512);
+  static constexpr uint32_t IDESC_S = idesc_i8(kBM, kBN, false);
+  static constexpr uint32_t IDESC_PV = idesc_i8(kBM, DV, true);
+  static constexpr uint32_t SWQ = QA == 32 ? kSw32 : (QA == 64 ? kSw64 : kSw128);
+  static constexpr uint32_t SWV = VA == 32 ? kSw32 : (VA == 64 ? kSw64 : kSw128);
+};
+
+template <int DQK, int DV, bool BIAS>
+__global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
+    qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
+                   const KArgs a) {
+  using C = Cfg<DQK, DV, BIAS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto q_full = [&](int i) { return bar0 + 8u * i; };
+  auto q_empty = [&](int i) { return bar0 + 8u * (2 + i); };
+  auto kv_full = [&](int i) { return bar0 + 8u * (4 + i); };
+  auto kv_empty = [&](int i) { return bar0 + 8u * (4 + C::KVS + i); };
+  auto s_full = [&](int i) { return bar0 + 8u * (4 + 2 * C::KVS + i); };
+  auto p_full = [&](int i) { return bar0 + 8u * (6 + 2 * C::KVS + i); };
+  auto pv_full = [&](int i) { return bar0 + 8u * (8 + 2 * C::KVS + i); };
+  auto pv_empty = [&](int i) { return bar0 + 8u * (10 + 2 * C::KVS + i); };
+  uint32_t* tmem_slot = (uint32_t*)(smem + C::OFF_MISC);
+  volatile int* abort_flag = (volatile int*)(smem + C::OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(q_full(i), 1);
+      mbar_init(q_empty(i), 1);
+      mbar_init(s_full(i), 1);
+      mbar_init(p_full(i), 4);
+      mbar_init(pv_full(i), 1);
+      mbar_init(pv_empty(i), 4);
+    }
+    for (int i = 0; i < C::KVS; ++i) {
+      mbar_init(kv_full(i), 1);
+      mbar_init(kv_empty(i), 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto fail = [&](unsigned code) {
+    atomicOr(&g_err, code);
+    *abort_flag = 1;
+  };
+  auto wait = [&](uint32_t bar, uint32_t parity, unsigned code) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        fail(code);
+        return false;
+      }
+    }
+    return true;
+  };
+
+  const int nch = a.nch;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      if (BIAS) tma_prefetch_desc(&tmB);
+      uint32_t kv_it = 0;
+      int qi = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x, ++qi) {
+        const int zh = item / a.ntiles, tile = item - zh * a.ntiles;
+        const int z = zh / a.H, h = zh - z * a.H;
+        const int qb = qi & 1;
+        if (!(ok = wait(q_empty(qb), ((qi >> 1) & 1) ^ 1, kErrQEmpty))) break;
+        mbar_arrive_expect_tx(q_full(qb), C::Q_BYTES);
+#pragma unroll
+        for (int at = 0; at < C::NQA; ++at)
+          tma_load_4d(sbase + C::OFF_Q + qb * C::Q_BYTES + at * kBM * C::QA, &tmQ, q_full(qb), at * C::QA,
+                      tile * kBM, h, z);
+        for (int j = 0; j < nch; ++j, ++kv_it) {
+          const int st = kv_it % C::KVS;
+          if (!(ok = wait(kv_empty(st), ((kv_it / C::KVS) & 1) ^ 1, kErrKvEmpty))) break;
+          mbar_arrive_expect_tx(kv_full(st), C::K_BYTES + C::V_BYTES + C::B_BYTES);
+#pragma unroll
+          for (int at = 0; at < C::NQA; ++at)
+            tma_load_4d(sbase + C::OFF_K + st * C::K_BYTES + at * kBN * C::QA, &tmK, kv_full(st), at * C::QA,
+                        j * kBN, h, z);
+          tma_load_4d(sbase + C::OFF_V + st * C::V_BYTES, &tmV, kv_full(st), a.v_col0, j * kBN, h, z);
+          if (BIAS)
+            tma_load_4d(sbase + C::OFF_B + st * C::B_BYTES, &tmB, kv_full(st), j * kBN, tile * kBM,
+                        a.bias_hb ? h : 0, a.bias_zb ? z : 0);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      uint32_t g = 0;
+      int qi = 0;
+      bool ok = true;
+      auto issue_pv = [&](uint32_t gg) -> bool {
+        const int slot = gg & 1;
+        const int st = gg % C::KVS;
+        if (!wait(p_full(slot), (gg >> 1) & 1, kErrPFull)) return false;
+        if (!wait(pv_empty(slot), ((gg >> 1) & 1) ^ 1, kErrPvEmpty)) return false;
+        tc_fence_after();
+        const uint64_t bdesc = smem_desc(sbase + C::OFF_V + st * C::V_BYTES, kBN * C::VA, 8 * C::VA, C::SWV);
+        mma_i8_ts(tmem + 64 + slot * DV, tmem + slot * 32, bdesc, C::IDESC_PV, 0);
+        tc_commit(pv_full(slot));
+        tc_commit(kv_empty(st));
+        return true;
+      };
+      for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x, ++qi) {
+        const int qb = qi & 1;
+        if (!(ok = wait(q_full(qb), (qi >> 1) & 1, kErrQFull))) break;
+        tc_fence_after();
+        const uint32_t qaddr = sbase + C::OFF_Q + qb * C::Q_BYTES;
+        for (int j = 0; j < nch; ++j, ++g) {
+          const int st = g % C::KVS;
+          if (!(ok = wait(kv_full(st), (g / C::KVS) & 1, kErrKvFull))) break;
+          tc_fence_after();
+          const uint32_t kaddr = sbase + C::OFF_K + st * C::K_BYTES;
+          const uint32_t dS = tmem + (g & 1) * 32;
+#pragma unroll
+          for (int kk = 0; kk < DQK / 32; ++kk) {
+            const int at = (kk * 32) / C::QA, off = (kk * 32) % C::QA;
+            const uint64_t ad = smem_desc(qaddr + at * kBM * C::QA + off, 16, 8 * C::QA, C::SWQ);
+            const uint64_t bd = smem_desc(kaddr + at * kBN * C::QA + off, 16, 8 * C::QA, C::SWQ);
+            mma_i8_ss(dS, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(s_full(g & 1));
+          if (j == nch - 1) tc_commit(q_empty(qb));
+          if (j > 0 && !(ok = issue_pv(g - 1))) break;
+        }
+        if (ok) ok = issue_pv(g - 1);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax warps
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const bool exp_idiv = a.flags & QFLASH_FLAG_EXP_IDIV;
+    const bool l_idiv = a.flags & QFLASH_FLAG_L_IDIV;
+    const bool acc_idiv = a.flags & QFLASH_FLAG_ACC_IDIV;
+    const bool div_full = a.flags & QFLASH_FLAG_DIV_FULL;
+    const bool fast_exp = a.fast_exp && !exp_idiv;
+    const int rs = a.rs, eM = a.eM, rM = a.rM;
+    const int S = a.as;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x) {
+      const int zh = item / a.ntiles, tile = item - zh * a.ntiles;
+      const int row0 = tile * kBM + warp * 32;
+      const bool active = row0 < a.N;
+      const int row = row0 + lane;
+      int m = kNegInf, l = 1, alpha_prev = 0;
+      uint32_t acc[DV];  // acc + 2^31 (biased)
+#pragma unroll
+      for (int d = 0; d < DV; ++d) acc[d] = 0x80000000u;
+
+      // acc = rescale(acc, alpha) + PV_gg
+      auto consume_pv = [&](uint32_t gg, int alpha) -> bool {
+        const int slot = gg & 1;
+        if (!wait(pv_full(slot), (gg >> 1) & 1, kErrPvFull)) return false;
+        tc_fence_after();
+        if (active) {
+          const long long A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
+          const bool fast = !acc_idiv && S < 32 && A >= 0 && A < (1ll << 32);
+          const bool all_fast = __all_sync(0xffffffffu, fast);
+          const unsigned long long Cst =
+              (1ull << (S - 1)) - ((unsigned long long)A << 31) + (1ull << ((S + 31) & 63));
+#pragma unroll
+          for (int part = 0; part < DV / 32; ++part) {
+            int pv[32];
+            tmem_ld32(tmem + lane_base + 64 + slot * DV + part * 32, pv);
+            if (all_fast) {
+              const uint32_t A32 = (uint32_t)A;
+#pragma unroll
+              for (int d = 0; d < 32; ++d) {
+                unsigned long long w;
+                asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(w) : "r"(acc[part * 32 + d]), "r"(A32), "l"(Cst));
+                const uint32_t res = __funnelshift_r((uint32_t)w, (uint32_t)(w >> 32), S);
+                acc[part * 32 + d] = res + (uint32_t)pv[d];
+              }
+            } else {
+#pragma unroll
+              for (int d = 0; d < 32; ++d) {
+                const int x = (int)(acc[part * 32 + d] ^ 0x80000000u);
+                const int r = acc_idiv ? rel_idiv(x, alpha, rs) : rel_shift64(x, (unsigned long long)A, S);
+                acc[part * 32 + d] = ((uint32_t)r + (uint32_t)pv[d]) ^ 0x80000000u;
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pv_empty(slot));
+        return true;
+      };
+
+      for (int j = 0; j < nch; ++j, ++g) {
+        const int slot = g & 1;
+        if (!(ok = wait(s_full(slot), (g >> 1) & 1, kErrSFull))) break;
+        tc_fence_after();
+        int alpha = 0;
+        if (active) {
+          int s[32];
+          tmem_ld32(tmem + lane_base + slot * 32, s);
+          if (BIAS) {
+            const uint8_t* brow = smem + C::OFF_B + (g % C::KVS) * C::B_BYTES + (warp * 32 + lane) * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int4 b = *(const int4*)(brow + ((c ^ (lane & 7)) << 4));
+              s[4 * c + 0] = (int)((unsigned)s[4 * c + 0] + (unsigned)b.x);
+              s[4 * c + 1] = (int)((unsigned)s[4 * c + 1] + (unsigned)b.y);
+              s[4 * c + 2] = (int)((unsigned)s[4 * c + 2] + (unsigned)b.z);
+              s[4 * c + 3] = (int)((unsigned)s[4 * c + 3] + (unsigned)b.w);
+            }
+          }
+          const int nvalid = a.N - j * kBN;
+          if (nvalid < kBN) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (c >= nvalid) s[c] = kNegInf;
+          }
+          int mx = s[0];
+#pragma unroll
+          for (int c = 1; c < 32; ++c) mx = max(mx, s[c]);
+          const int m_new = max(m, mx);
+          uint32_t pw[8];
+          int lsum = 0;
+          if (fast_exp) {
+            const int cm1 = (int)((0u - (unsigned)m_new) * (unsigned)eM + 65536u);
+            const int c3 = (int)((unsigned)rs - (unsigned)m_new);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int e0 = exp2_fast(s[4 * c + 0], eM, cm1, rs, c3);
+              const int e1 = exp2_fast(s[4 * c + 1], eM, cm1, rs, c3);
+              const int e2 = exp2_fast(s[4 * c + 2], eM, cm1, rs, c3);
+              const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
+              pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+              lsum = __dp4a((int)pw[c], 0x01010101, lsum);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int e0 = exp2_generic((int)((unsigned)s[4 * c + 0] - (unsigned)m_new), rs, eM, exp_idiv);
+              const int e1 = exp2_generic((int)((unsigned)s[4 * c + 1] - (unsigned)m_new), rs, eM, exp_idiv);
+              const int e2 = exp2_generic((int)((unsigned)s[4 * c + 2] - (unsigned)m_new), rs, eM, exp_idiv);
+              const int e3 = exp2_generic((int)((unsigned)s[4 * c + 3] - (unsigned)m_new), rs, eM, exp_idiv);
+              pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+              lsum = __dp4a((int)pw[c], 0x01010101, lsum);
+            }
+          }
+          alpha = exp2_generic((int)((unsigned)m - (unsigned)m_new), rs, eM, exp_idiv);
+          tmem_st8(tmem + lane_base + slot * 32, pw);
+          const int lr = l_idiv ? rel_idiv(l, alpha, rs)
+                                : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
+          l = (int)((unsigned)lr + (unsigned)lsum);
+          m = m_new;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(slot));
+        if (j > 0 && !(ok = consume_pv(g - 1, alpha_prev))) break;
+        alpha_prev = alpha;
+      }
+      if (!ok) break;
+      if (!(ok = consume_pv(g - 1, alpha_prev))) break;
+
+      // epilogue: O row = int8(int32(fp32(acc) / fp32(l)))
+      if (active && row < a.N) {
+        const int z = zh / a.H, h = zh - z * a.H;
+        int8_t* orow = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row * a.os_n + a.v_col0;
+#pragma unroll
+        for (int c = 0; c < DV / 16; ++c) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            int r4[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) r4[b] = div_to_i32((int)(acc[c * 16 + w4 * 4 + b] ^ 0x80000000u), l, div_full);
+            wv[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
+          }
+          if (a.o_vec16) {
+            *(int4*)(orow + c * 16) = make_int4((int)wv[0], (int)wv[1], (int)wv[2], (int)wv[3]);
+          } else {
+#pragma unroll
+            for (int b = 0; b < 16; ++b) orow[c * 16 + b] = (int8_t)(wv[b >> 2] >> (8 * (b & 3)));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static thread_local std::string t_err;
+static std::atomic<uint64_t> g_launches{0};
+
+static int set_err(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  });
+  return fn;
+}
+
+static CUtensorMapSwizzle tma_swizzle(int atom_bytes) {
+  return atom_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                          : (atom_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// 4-D map over a [Z, H, rows, cols] tensor (cols contiguous); strides in bytes.
+static int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t cols, uint64_t rows,
+                    uint64_t H, uint64_t Z, uint64_t s_row, uint64_t s_h, uint64_t s_z, uint32_t box_cols,
+                    uint32_t box_rows, int atom_bytes) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_err(QFLASH_ERR_DEVICE, "cuTensorMapEncodeTiled entry point unavailable");
+  if (((uintptr_t)base & 15) || (s_row & 15) || (s_h & 15) || (s_z & 15))
+    return set_err(QFLASH_ERR_ALIGN, "TMA needs 16-byte aligned base and strides (base %p, strides %llu %llu %llu)",
+                   base, (unsigned long long)s_row, (unsigned long long)s_h, (unsigned long long)s_z);
+  cuuint64_t dims[4] = {cols, rows, H, Z};
+  cuuint64_t strides[3] = {s_row, s_h, s_z};
+  cuuint32_t box[4] = {box_cols, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   tma_swizzle(atom_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_err(QFLASH_ERR_TMA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QFLASH_OK;
+}
+
+constexpr int kMaxDevices = 64;
+
+static int sm_count(int dev) {
+  static int n[kMaxDevices] = {0};
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev];
+}
+
+template <int DQK, int DV, bool BIAS>
+static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                  const CUtensorMap& mb, const KArgs& ka, cudaStream_t stream) {
+  using C = Cfg<DQK, DV, BIAS>;
+  auto kern = qfa_fwd_kernel<DQK, DV, BIAS>;
+  static int per_sm[kMaxDevices] = {0};
+  static std::mutex mu;
+  int ctas;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (per_sm[dev] == 0) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+        return set_err(QFLASH_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError()));
+      int occ = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, C::SMEM);
+      const int by_tmem = 512 / C::TMEM_COLS;
+      int v = occ < by_tmem ? occ : by_tmem;
+      per_sm[dev] = v < 1 ? 1 : v;
+    }
+    ctas = per_sm[dev];
+  }
+  int grid = sm_count(dev) * ctas;
+  if (grid > ka.nitems) grid = ka.nitems;
+  kern<<<grid, kThreads, C::SMEM, stream>>>(mq, mk, mv, mb, ka);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return QFLASH_OK;
+}
+
+// Make the device that owns `p` current for this library's runtime (its
+// current-device state is separate from the caller's).
+static int select_device(const void* p, int* dev) {
+  cudaPointerAttributes pa;
+  if (cudaPointerGetAttributes(&pa, p) != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(QFLASH_ERR_ARG, "pointer %p is not known to CUDA", p);
+  }
+  if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
+    return set_err(QFLASH_ERR_ARG, "pointer %p is not device memory", p);
+  if (pa.device < 0 || pa.device >= kMaxDevices) return set_err(QFLASH_ERR_DEVICE, "device %d", pa.device);
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != pa.device && cudaSetDevice(pa.device) != cudaSuccess)
+    return set_err(QFLASH_ERR_DEVICE, "cudaSetDevice(%d) failed", pa.device);
+  static int checked[kMaxDevices] = {0};
+  if (!checked[pa.device]) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, pa.device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, pa.device);
+    if (major != 10 || minor != 0)
+      return set_err(QFLASH_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", pa.device, major,
+                     minor);
+    checked[pa.device] = 1;
+  }
+  *dev = pa.device;
+  return QFLASH_OK;
+}
+
+}  // namespace qfb
+
+using namespace qfb;
+
+extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                             const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                             const int64_t o_strides[4], const int64_t bias_strides[4], int Z, int H, int N, int D,
+                             int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
+                             int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream_) {
+  cudaStream_t stream = (cudaStream_t)stream_;
+  if (Z < 0 || H < 0 || N < 0) return set_err(QFLASH_ERR_ARG, "negative shape");
+  if (!(D == 32 || D == 64 || D == 128 || D == 256)) return set_err(QFLASH_ERR_ARG, "head dim %d not in {32,64,128,256}", D);
+  if (Z == 0 || H == 0 || N == 0) return QFLASH_OK;
+  if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides)
+    return set_err(QFLASH_ERR_ARG, "null pointer");
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || o_strides[3] != 1)
+    return set_err(QFLASH_ERR_ARG, "innermost (head-dim) stride must be 1");
+  if (sm_rscale <= 0) return set_err(QFLASH_ERR_ARG, "sm_rscale must be positive");
+  if (l_shift < 1 || l_shift > 62 || acc_shift < 1 || acc_shift > 62) return set_err(QFLASH_ERR_ARG, "shift out of [1, 62]");
+  if (bias && !bias_strides) return set_err(QFLASH_ERR_ARG, "bias without strides");
+  int dev = 0;
+  if (int rc0 = select_device(q, &dev)) return rc0;
+
+  KArgs ka;
+  memset(&ka, 0, sizeof(ka));
+  ka.Z = Z;
+  ka.H = H;
+  ka.N = N;
+  ka.nch = (N + kBN - 1) / kBN;
+  ka.ntiles = (N + kBM - 1) / kBM;
+  const long long items = (long long)Z * H * ka.ntiles;
+  if (items > 0x7fffffffLL) return set_err(QFLASH_ERR_ARG, "too many tiles");
+  ka.nitems = (int)items;
+  ka.o = o;
+  ka.os_z = o_strides[0];
+  ka.os_h = o_strides[1];
+  ka.os_n = o_strides[2];
+  ka.o_vec16 = (((uintptr_t)o & 15) == 0) && (o_strides[0] % 16 == 0) && (o_strides[1] % 16 == 0) &&
+               (o_strides[2] % 16 == 0);
+  ka.rs = sm_rscale;
+  ka.eM = exp_M;
+  ka.rM = req_M;
+  ka.lM = l_M;
+  ka.accM = acc_M;
+  ka.ls = l_shift;
+  ka.as = acc_shift;
+  ka.flags = flags;
+  // The 6-op exp2 form (exp2_fast) is exact when no int32 value in it wraps.
+  // Without a bias a score lies in [-D*2^14, D*2^14] (int8 dot products) or is
+  // NEG_INF, the running max in [NEG_INF, D*2^14], so |x| <= xmax below; then
+  // |t1| <= |exp_M|*xmax + 2^16 and |r2| <= xmax*(|exp_M|*rs/2^16 + 1) + 2*rs.
+  {
+    const long long smax = (long long)D << 14;
+    const long long xmax = (smax > (1ll << 20) ? smax : (1ll << 20)) + smax;
+    const long long aem = -(long long)exp_M;
+    const bool ok1 = aem * xmax + 65536 < (1ll << 31);
+    const bool ok2 = (xmax * (aem * sm_rscale + 65536)) / 65536 + 1 + 2ll * sm_rscale < (1ll << 31);
+    ka.fast_exp = (!bias && exp_M <= 0 && ok1 && ok2) ? 1 : 0;
+  }
+
+  const int DV = D == 256 ? 128 : D;
+  const int qa = D < 128 ? D : 128;
+  CUtensorMap mq, mk, mv, mb;
+  memset(&mb, 0, sizeof(mb));
+  int rc;
+  if ((rc = make_map(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, D, N, H, Z, q_strides[2], q_strides[1], q_strides[0], qa,
+                     kBM, qa)))
+    return rc;
+  if ((rc = make_map(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, D, N, H, Z, k_strides[2], k_strides[1], k_strides[0], qa,
+                     kBN, qa)))
+    return rc;
+  if ((rc = make_map(&mv, CU_TENSOR_MAP_DATA_TYPE_UINT8, v, D, N, H, Z, v_strides[2], v_strides[1], v_strides[0], DV,
+                     kBN, DV)))
+    return rc;
+  if (bias) {
+    const int64_t bz = bias_strides[0], bh = bias_strides[1], br = bias_strides[2], bc = bias_strides[3];
+    if (bc != 1) return set_err(QFLASH_ERR_ARG, "bias innermost stride must be 1");
+    ka.bias_zb = bz != 0;
+    ka.bias_hb = bh != 0;
+    const uint64_t row_b = (uint64_t)br * 4;
+    const uint64_t h_b = bh ? (uint64_t)bh * 4 : row_b * N;
+    const uint64_t z_b = bz ? (uint64_t)bz * 4 : h_b * (bh ? H : 1);
+    if ((rc = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_INT32, bias, N, N, bh ? H : 1, bz ? Z : 1, row_b, h_b, z_b, kBN,
+                       kBM, 128)))
+      return rc;
+  }
+  const int passes = D == 256 ? 2 : 1;
+  for (int p = 0; p < passes; ++p) {
+    ka.v_col0 = p * DV;
+    if (bias) {
+      switch (D) {
+        case 32: rc = launch<32, 32, true>(dev, mq, mk, mv, mb, ka, stream); break;
+        case 64: rc = launch<64, 64, true>(dev, mq, mk, mv, mb, ka, stream); break;
+        case 128: rc = launch<128, 128, true>(dev, mq, mk, mv, mb, ka, stream); break;
+        default: rc = launch<256, 128, true>(dev, mq, mk, mv, mb, ka, stream); break;
+      }
+    } else {
+      switch (D) {
+        case 32: rc = launch<32, 32, false>(dev, mq, mk, mv, mb, ka, stream); break;
+        case 64: rc = launch<64, 64, false>(dev, mq, mk, mv, mb, ka, stream); break;
+        case 128: rc = launch<128, 128, false>(dev, mq, mk, mv, mb, ka, stream); break;
+        default: rc = launch<256, 128, false>(dev, mq, mk, mv, mb, ka, stream); break;
+      }
+    }
+    if (rc) return rc;
+  }
+  return QFLASH_OK;
+}
+
+extern "C" int qflash_device_error(void* stream, uint32_t* out) {
+  if (!out) return set_err(QFLASH_ERR_ARG, "null out");
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "sync: %s", cudaGetErrorString(e));
+  unsigned v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_err, sizeof(v)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_err, &zero, sizeof(zero)) != cudaSuccess)
+    return set_err(QFLASH_ERR_LAUNCH, "error word: %s", cudaGetErrorString(cudaGetLastError()));
+  *out = v;
+  return QFLASH_OK;
+}
+
+extern "C" uint64_t qflash_launch_count(void) { return g_launches.load(); }
+extern "C" const char* qflash_version(void) { return "qflash_b200 0.1.0 (sm_100a)"; }
+extern "C" const char* qflash_last_error(void) { return t_err.c_str(); }

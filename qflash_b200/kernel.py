@@ -1,0 +1,214 @@
+"""``qflash.forward``: QFlash's integer-only attention forward on B200.
+
+Host side of the drop-in replacement for qflash/kernel.py:275-356.  The host
+math (scale derivation, fixed-point constants in Python doubles, per-tensor
+int8 quantisation, bias quantisation) follows the reference step for step so
+that the int8 tensors and constants the kernel receives are bit-identical;
+the two Triton launches are replaced by one call into the C ABI
+(``qflash_i8_fwd``, include/qflash_b200.h) whose sm_100a kernel computes the
+same int8 output.
+
+Environment flags, read once at import like the reference (kernel.py:30-36):
+QFLASH_EXP_USE_SHIFT, QFLASH_L_USE_SHIFT, QFLASH_ACC_USE_SHIFT (default 1),
+QFLASH_L_SHIFT, QFLASH_ACC_SHIFT (default 30).  QFLASH_AUTOTUNE and
+QFLASH_CUDA_GRAPH are accepted; they only pick Triton launch configurations
+there and change no arithmetic, and this kernel has a single configuration.
+QFLASH_DIV selects the rounding of the final fp32 division acc / l:
+"ieee" (default; the reference's integer path as specified and as its
+interpreted run computes it) or "full" (the approximate fp32 divide that the
+reference's compiled GPU kernel uses).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+AUTOTUNE_SETTING = os.environ.get("QFLASH_AUTOTUNE", "default")
+USE_CUDA_GRAPH = os.environ.get("QFLASH_CUDA_GRAPH", "0") == "1"
+EXP_USE_SHIFT = os.environ.get("QFLASH_EXP_USE_SHIFT", "1") == "1"
+L_USE_SHIFT = os.environ.get("QFLASH_L_USE_SHIFT", "1") == "1"
+ACC_USE_SHIFT = os.environ.get("QFLASH_ACC_USE_SHIFT", "1") == "1"
+L_SHIFT = int(os.environ.get("QFLASH_L_SHIFT", "30"))
+ACC_SHIFT = int(os.environ.get("QFLASH_ACC_SHIFT", "30"))
+DIV_MODE = os.environ.get("QFLASH_DIV", "ieee")
+
+LOG2E = 1.44269504
+NEG_INF = -(1 << 20)
+SHIFT = 16
+
+
+def arith_flags(exp_use_shift=None, l_use_shift=None, acc_use_shift=None, div_mode=None) -> int:
+    """C-ABI flag word for the QFLASH_* arithmetic switches."""
+    f = 0
+    if not (EXP_USE_SHIFT if exp_use_shift is None else exp_use_shift):
+        f |= _lib.FLAG_EXP_IDIV
+    if not (L_USE_SHIFT if l_use_shift is None else l_use_shift):
+        f |= _lib.FLAG_L_IDIV
+    if not (ACC_USE_SHIFT if acc_use_shift is None else acc_use_shift):
+        f |= _lib.FLAG_ACC_IDIV
+    mode = DIV_MODE if div_mode is None else div_mode
+    if mode not in ("ieee", "full"):
+        raise ValueError(f"QFLASH_DIV must be 'ieee' or 'full', got {mode!r}")
+    if mode == "full":
+        f |= _lib.FLAG_DIV_FULL
+    return f
+
+
+def fixed_point_params(qk_scale: float, head_dim: int, scale: float | None,
+                       l_shift: int = None, acc_shift: int = None):
+    """qflash/kernel.py:290-307 in Python doubles: returns
+    (sm_scale, sm_rscale, exp_M, req_M, l_M, acc_M)."""
+    l_shift = L_SHIFT if l_shift is None else l_shift
+    acc_shift = ACC_SHIFT if acc_shift is None else acc_shift
+    if scale is None:
+        scale = 1.0 / (head_dim ** 0.5)
+    scale = scale * LOG2E
+    sm_scale = scale * qk_scale
+    sm_rscale = int(round(1.0 / sm_scale))
+    exp_M = int(round(-sm_scale * (1 << SHIFT)))
+    req_M = int(round(sm_scale * 127 * (1 << SHIFT)))
+    l_M = int(round((1 << l_shift) / sm_rscale))
+    acc_M = int(round((1 << acc_shift) / sm_rscale))
+    return sm_scale, sm_rscale, exp_M, req_M, l_M, acc_M
+
+
+def quantize(x: Tensor, s: Tensor) -> Tensor:
+    """qflash/kernel.py:309-311: int8(clamp(round(x / s), -128, 127))."""
+    return torch.clamp(torch.round(x / s), -128, 127).to(torch.int8)
+
+
+def quantize_bias(attn_mask: Tensor, sm_scale: float, Z: int, H: int, N: int):
+    """qflash/kernel.py:328-336 without the .expand().contiguous() copy.
+
+    The same torch ops run on the mask at its own (broadcastable) shape --
+    elementwise ops commute with broadcasting, so every value equals the
+    reference's -- and the result is laid out as [Zb, Hb, N, N4] int32 with
+    the row pitch N4 padded to a multiple of 4 (16 bytes, a TMA requirement).
+    Returns (bias, element strides with 0 on broadcast dimensions).
+    """
+    if attn_mask.dtype == torch.bool:
+        bias = torch.where(attn_mask, 0, NEG_INF).to(torch.int32)
+    else:
+        is_masked = attn_mask < -1e2
+        clipped = attn_mask.masked_fill(is_masked, 0.0)
+        quant = (clipped * LOG2E / sm_scale).round().to(torch.int32)
+        bias = quant.masked_fill(is_masked, NEG_INF)
+    while bias.dim() < 4:
+        bias = bias.unsqueeze(0)
+    if bias.dim() != 4:
+        raise ValueError(f"attn_mask must broadcast to (Z, H, N, N); got shape {tuple(attn_mask.shape)}")
+    Zb = Z if bias.shape[0] != 1 else 1
+    Hb = H if bias.shape[1] != 1 else 1
+    bias = bias.expand(Zb, Hb, N, N)
+    N4 = (N + 3) // 4 * 4
+    out = torch.empty((Zb, Hb, N, N4), dtype=torch.int32, device=bias.device)
+    out[..., :N].copy_(bias)
+    st = out.stride()
+    return out, [st[0] if Zb > 1 else 0, st[1] if Hb > 1 else 0, st[2], 1]
+
+
+def do_bench(fn, warmup: float = 10, rep: float = 100) -> float:
+    """Median kernel time in ms: warm-up and repetition budgets in ms, the L2
+    flushed (256 MB written) before every timed run, CUDA events around each
+    run -- the method of the reference's latency mode (kernel.py:348-349)."""
+    fn()
+    torch.cuda.synchronize()
+    cache = torch.empty(int(256e6 // 4), dtype=torch.int32, device="cuda")
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(5):
+        cache.zero_()
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    est = s.elapsed_time(e) / 5
+    n_warm = max(1, int(warmup / est))
+    n_rep = max(1, int(rep / est))
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n_rep)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n_rep)]
+    for _ in range(n_warm):
+        fn()
+    for i in range(n_rep):
+        cache.zero_()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    times = sorted(a.elapsed_time(b) for a, b in zip(starts, ends))
+    return times[len(times) // 2] if len(times) % 2 else 0.5 * (times[len(times) // 2 - 1] + times[len(times) // 2])
+
+
+def launch_int8(q8: Tensor, k8: Tensor, v8: Tensor, o8: Tensor, sm_rscale: int, exp_M: int, req_M: int,
+                l_M: int, acc_M: int, bias: Tensor | None = None, bias_strides=None,
+                l_shift: int = None, acc_shift: int = None, flags: int = None, stream=None) -> None:
+    """Run the sm_100a kernel on int8 [Z, H, N, D] tensors already on the GPU
+    (the launch at qflash/kernel.py:319-326 / 339-346)."""
+    for t in (q8, k8, v8, o8):
+        if not t.is_cuda or t.dtype != torch.int8 or t.dim() != 4:
+            raise ValueError("q, k, v, o must be 4-D int8 CUDA tensors")
+    Z, H, N, D = q8.shape
+    if stream is None:
+        stream = torch.cuda.current_stream(q8.device).cuda_stream
+    for name, val in (("exp_M", exp_M), ("req_M", req_M), ("sm_rscale", sm_rscale)):
+        if not -(1 << 31) <= val < (1 << 31):
+            raise OverflowError(f"{name}={val} does not fit in int32")
+    _lib.i8_fwd(q8, k8, v8, o8, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
+                L_SHIFT if l_shift is None else l_shift, ACC_SHIFT if acc_shift is None else acc_shift,
+                arith_flags() if flags is None else flags, stream)
+
+
+def qflash_forward(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    attn_mask: Tensor | None = None,
+    scale: float | None = None,
+    return_mode: str = 'output',
+):
+    """Integer-only attention; same signature, arithmetic and output dtype as
+    the reference's ``qflash.forward`` (qflash/kernel.py:275-351)."""
+    HEAD_DIM_Q, HEAD_DIM_K = query.shape[-1], key.shape[-1]
+    HEAD_DIM_V = value.shape[-1]
+    assert HEAD_DIM_Q == HEAD_DIM_K and HEAD_DIM_K == HEAD_DIM_V
+    assert HEAD_DIM_K in {16, 32, 64, 128, 256}
+    if HEAD_DIM_K == 16:
+        # the reference fails to compile here: tl.static_assert(BLOCK_N <= HEAD_DIM), BLOCK_N = 32
+        raise ValueError("head dim 16 is not supported (the chunk width 32 exceeds it), as in the reference")
+    if not (query.is_cuda and key.is_cuda and value.is_cuda):
+        raise ValueError("qflash.forward runs on CUDA tensors only")
+
+    q_scale = query.abs().amax() / torch.iinfo(torch.int8).max
+    k_scale = key.abs().amax() / torch.iinfo(torch.int8).max
+    o_scale = value.abs().amax() / torch.iinfo(torch.int8).max
+    qk_scale = (q_scale * k_scale).item()
+    sm_scale, sm_rscale, exp_M, req_M, l_M, acc_M = fixed_point_params(qk_scale, HEAD_DIM_Q, scale)
+
+    query = quantize(query, q_scale)
+    key = quantize(key, k_scale)
+    value = quantize(value, o_scale)
+    # the TMA loads need the head dim innermost (the reference takes any strides)
+    query, key, value = (t if t.stride(-1) == 1 else t.contiguous() for t in (query, key, value))
+    o = torch.empty_like(value)
+
+    Z, H, N = query.shape[0], query.shape[1], query.shape[2]
+    bias, bias_strides = None, None
+    if attn_mask is not None:
+        bias, bias_strides = quantize_bias(attn_mask, sm_scale, Z, H, N)
+
+    def kernel():
+        launch_int8(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides)
+
+    if return_mode == 'latency':
+        return do_bench(kernel, warmup=10, rep=100)
+    kernel()
+    return o * o_scale
+
+
+class qflash:
+    """The reference's public op class (qflash/kernel.py:354-356)."""
+    kernel = [launch_int8]
+    forward = qflash_forward
