@@ -66,6 +66,9 @@ int qflash_device_error(void* stream, uint32_t* out);
 /* Number of kernel launches issued by this library since load (for accounting). */
 uint64_t qflash_launch_count(void);
 
+/* Grid size (CTAs) of the most recent kernel launch (for accounting). */
+int qflash_last_grid(void);
+
 /* Library version string. */
 const char* qflash_version(void);
 

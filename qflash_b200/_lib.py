@@ -31,6 +31,7 @@ SIGNATURES = {
         ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p]),
     "qflash_device_error": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "qflash_launch_count": (ctypes.c_uint64, []),
+    "qflash_last_grid": (ctypes.c_int, []),
     "qflash_version": (ctypes.c_char_p, []),
     "qflash_last_error": (ctypes.c_char_p, []),
 }
@@ -90,3 +91,7 @@ def device_error(stream) -> int:
 
 def launch_count() -> int:
     return int(load().qflash_launch_count())
+
+
+def last_grid() -> int:
+    return int(load().qflash_last_grid())

@@ -27,6 +27,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -159,7 +160,9 @@ struct Cfg {
   static constexpr uint32_t SWV = VA == 32 ? kSw32 : (VA == 64 ? kSw64 : kSw128);
 };
 
-template <int DQK, int DV, bool BIAS>
+// GEN = false: the reference's default arithmetic (shift forms; flags other
+// than DIV_FULL must be 0), compact code.  GEN = true: every QFLASH_* mode.
+template <int DQK, int DV, bool BIAS, bool GEN>
 __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
     qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
@@ -308,13 +311,17 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
   } else {
     // ---------------------------------------------------------------- softmax warps
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const bool exp_idiv = a.flags & QFLASH_FLAG_EXP_IDIV;
-    const bool l_idiv = a.flags & QFLASH_FLAG_L_IDIV;
-    const bool acc_idiv = a.flags & QFLASH_FLAG_ACC_IDIV;
+    const bool exp_idiv = GEN && (a.flags & QFLASH_FLAG_EXP_IDIV);
+    const bool l_idiv = GEN && (a.flags & QFLASH_FLAG_L_IDIV);
+    const bool acc_idiv = GEN && (a.flags & QFLASH_FLAG_ACC_IDIV);
     const bool div_full = a.flags & QFLASH_FLAG_DIV_FULL;
-    const bool fast_exp = a.fast_exp && !exp_idiv;
+    constexpr bool kFastExp = !GEN && !BIAS;  // host guarantees the exp2_fast conditions
     const int rs = a.rs, eM = a.eM, rM = a.rM;
     const int S = a.as;
+    // rescaling by alpha == rs is the identity while |acc| * |delta0| < 2^(S-1)
+    const long long delta0 = (long long)rs * a.accM - (1ll << S);
+    const float ident_lim = (float)(1ull << (S - 1)) * 0.999f / (float)(delta0 < 0 ? -delta0 : (delta0 ? delta0 : 1));
+    const float two_mS = __int_as_float((127 - S) << 23);  // 2^-S
     uint32_t g = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x) {
@@ -322,36 +329,54 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       const int row0 = tile * kBM + warp * 32;
       const bool active = row0 < a.N;
       const int row = row0 + lane;
+      const bool row_ok = row < a.N;
       int m = kNegInf, l = 1, alpha_prev = 0;
+      // upper bound on max |acc| of this row, kept in fp32 with round-up margins
+      float abound = 0.f;
       uint32_t acc[DV];  // acc + 2^31 (biased)
 #pragma unroll
       for (int d = 0; d < DV; ++d) acc[d] = 0x80000000u;
 
-      // acc = rescale(acc, alpha) + PV_gg
-      auto consume_pv = [&](uint32_t gg, int alpha) -> bool {
+      // acc = rescale(acc, alpha) + PV_gg; `first`: acc is still all zero
+      auto consume_pv = [&](uint32_t gg, int alpha, bool first) -> bool {
         const int slot = gg & 1;
         if (!wait(pv_full(slot), (gg >> 1) & 1, kErrPvFull)) return false;
         tc_fence_after();
         if (active) {
           const long long A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
+          const bool ident = !acc_idiv && alpha == rs && abound < ident_lim;
+          const bool skip = first || __all_sync(0xffffffffu, ident || !row_ok);
           const bool fast = !acc_idiv && S < 32 && A >= 0 && A < (1ll << 32);
-          const bool all_fast = __all_sync(0xffffffffu, fast);
-          const unsigned long long Cst =
-              (1ull << (S - 1)) - ((unsigned long long)A << 31) + (1ull << ((S + 31) & 63));
+          const int mode = skip ? 0 : (__all_sync(0xffffffffu, fast) ? 1 : 2);
+          const uint32_t base = tmem + lane_base + 64 + slot * DV;
+          if (mode == 0) {
 #pragma unroll
-          for (int part = 0; part < DV / 32; ++part) {
-            int pv[32];
-            tmem_ld32(tmem + lane_base + 64 + slot * DV + part * 32, pv);
-            if (all_fast) {
-              const uint32_t A32 = (uint32_t)A;
+            for (int part = 0; part < DV / 32; ++part) {
+              int pv[32];
+              tmem_ld32(base + part * 32, pv);
+#pragma unroll
+              for (int d = 0; d < 32; ++d) acc[part * 32 + d] += (uint32_t)pv[d];
+            }
+          } else if (mode == 1) {
+            const unsigned long long Cst =
+                (1ull << (S - 1)) - ((unsigned long long)A << 31) + (1ull << ((S + 31) & 63));
+            const uint32_t A32 = (uint32_t)A;
+#pragma unroll
+            for (int part = 0; part < DV / 32; ++part) {
+              int pv[32];
+              tmem_ld32(base + part * 32, pv);
 #pragma unroll
               for (int d = 0; d < 32; ++d) {
                 unsigned long long w;
                 asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(w) : "r"(acc[part * 32 + d]), "r"(A32), "l"(Cst));
-                const uint32_t res = __funnelshift_r((uint32_t)w, (uint32_t)(w >> 32), S);
-                acc[part * 32 + d] = res + (uint32_t)pv[d];
+                acc[part * 32 + d] = __funnelshift_r((uint32_t)w, (uint32_t)(w >> 32), S) + (uint32_t)pv[d];
               }
-            } else {
+            }
+          } else {
+#pragma unroll
+            for (int part = 0; part < DV / 32; ++part) {
+              int pv[32];
+              tmem_ld32(base + part * 32, pv);
 #pragma unroll
               for (int d = 0; d < 32; ++d) {
                 const int x = (int)(acc[part * 32 + d] ^ 0x80000000u);
@@ -360,6 +385,15 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
               }
             }
           }
+          // |rel(x)| <= |x| * |A| / 2^S + 1 (the idiv form: <= |x| * |alpha| / rs + 1)
+          // (no bound when a 64-bit product could wrap or in the idiv form)
+          if (!first) {
+            const float aAbs = fabsf((float)A);
+            abound = (acc_idiv || S > 31 || abound * aAbs >= 4.6e18f)
+                         ? __int_as_float(0x7f800000)
+                         : __fmaf_ru(abound, aAbs * two_mS * 1.0001f, 2.f);
+          }
+          abound = __fadd_ru(abound, 524288.f);  // + 2^19
         }
         tc_fence_before();
         __syncwarp();
@@ -386,19 +420,23 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
               s[4 * c + 3] = (int)((unsigned)s[4 * c + 3] + (unsigned)b.w);
             }
           }
-          const int nvalid = a.N - j * kBN;
+          const int nvalid = a.N - j * kBN;  // < 32 only in a ragged last chunk
           if (nvalid < kBN) {
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (c >= nvalid) s[c] = kNegInf;
+            for (int c = 0; c < 32; ++c) s[c] = c < nvalid ? s[c] : kNegInf;
           }
-          int mx = s[0];
+          // row max as a tree (depth 5)
+          int t16[16];
 #pragma unroll
-          for (int c = 1; c < 32; ++c) mx = max(mx, s[c]);
+          for (int c = 0; c < 16; ++c) t16[c] = max(s[c], s[c + 16]);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) t16[c] = max(t16[c], t16[c + 8]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) t16[c] = max(t16[c], t16[c + 4]);
+          const int mx = max(max(t16[0], t16[2]), max(t16[1], t16[3]));
           const int m_new = max(m, mx);
           uint32_t pw[8];
-          int lsum = 0;
-          if (fast_exp) {
+          if (kFastExp) {
             const int cm1 = (int)((0u - (unsigned)m_new) * (unsigned)eM + 65536u);
             const int c3 = (int)((unsigned)rs - (unsigned)m_new);
 #pragma unroll
@@ -408,7 +446,6 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
               const int e2 = exp2_fast(s[4 * c + 2], eM, cm1, rs, c3);
               const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
               pw[c] = requant_pack4(e0, e1, e2, e3, rM);
-              lsum = __dp4a((int)pw[c], 0x01010101, lsum);
             }
           } else {
 #pragma unroll
@@ -418,44 +455,75 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
               const int e2 = exp2_generic((int)((unsigned)s[4 * c + 2] - (unsigned)m_new), rs, eM, exp_idiv);
               const int e3 = exp2_generic((int)((unsigned)s[4 * c + 3] - (unsigned)m_new), rs, eM, exp_idiv);
               pw[c] = requant_pack4(e0, e1, e2, e3, rM);
-              lsum = __dp4a((int)pw[c], 0x01010101, lsum);
             }
           }
           alpha = exp2_generic((int)((unsigned)m - (unsigned)m_new), rs, eM, exp_idiv);
           tmem_st8(tmem + lane_base + slot * 32, pw);
+          // l_j = sum of the 32 int8 P values, two independent dot-product chains
+          int ls0 = 0, ls1 = 0;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            ls0 = __dp4a((int)pw[2 * c], 0x01010101, ls0);
+            ls1 = __dp4a((int)pw[2 * c + 1], 0x01010101, ls1);
+          }
           const int lr = l_idiv ? rel_idiv(l, alpha, rs)
                                 : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
-          l = (int)((unsigned)lr + (unsigned)lsum);
+          l = (int)((unsigned)lr + (unsigned)ls0 + (unsigned)ls1);
           m = m_new;
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(slot));
-        if (j > 0 && !(ok = consume_pv(g - 1, alpha_prev))) break;
+        if (j > 0 && !(ok = consume_pv(g - 1, alpha_prev, j == 1))) break;
         alpha_prev = alpha;
       }
       if (!ok) break;
-      if (!(ok = consume_pv(g - 1, alpha_prev))) break;
+      if (!(ok = consume_pv(g - 1, alpha_prev, nch == 1))) break;
 
       // epilogue: O row = int8(int32(fp32(acc) / fp32(l)))
-      if (active && row < a.N) {
+      if (active) {
         const int z = zh / a.H, h = zh - z * a.H;
         int8_t* orow = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row * a.os_n + a.v_col0;
+        // Exact shortcut: for |acc| < 2^23 and 0 < l < 2^24, trunc(RN_f32(acc / l))
+        // equals the truncated integer quotient (rounding up to an integer n >= 2
+        // needs l >= 2^24 / n, i.e. |acc| >= 2^23).  The quotient is a rounded
+        // float estimate (off by at most one) fixed by an exact remainder check.
+        const bool fast_div = !div_full && l > 0 && l < (1 << 24) && abound < 8388607.f;
+        uint32_t res[DV / 4];
+        if (__all_sync(0xffffffffu, fast_div || !row_ok)) {
+          const float rcp = __frcp_rn((float)l);
 #pragma unroll
-        for (int c = 0; c < DV / 16; ++c) {
-          uint32_t wv[4];
-#pragma unroll
-          for (int w4 = 0; w4 < 4; ++w4) {
+          for (int w4 = 0; w4 < DV / 4; ++w4) {
             int r4[4];
 #pragma unroll
-            for (int b = 0; b < 4; ++b) r4[b] = div_to_i32((int)(acc[c * 16 + w4 * 4 + b] ^ 0x80000000u), l, div_full);
-            wv[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
+            for (int b = 0; b < 4; ++b) {
+              const int x = (int)(acc[w4 * 4 + b] ^ 0x80000000u);
+              const int ux = abs(x);
+              const float af = __int_as_float(ux | 0x4B000000) - 8388608.0f;
+              int qd = __float_as_int(__fmaf_rn(af, rcp, 8388608.0f)) - 0x4B000000;
+              qd += (ux - qd * l) >> 31;
+              r4[b] = x < 0 ? -qd : qd;
+            }
+            res[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
           }
+        } else {
+#pragma unroll
+          for (int w4 = 0; w4 < DV / 4; ++w4) {
+            int r4[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) r4[b] = div_to_i32((int)(acc[w4 * 4 + b] ^ 0x80000000u), l, div_full);
+            res[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
+          }
+        }
+        if (row_ok) {
           if (a.o_vec16) {
-            *(int4*)(orow + c * 16) = make_int4((int)wv[0], (int)wv[1], (int)wv[2], (int)wv[3]);
+#pragma unroll
+            for (int c = 0; c < DV / 16; ++c)
+              *(int4*)(orow + c * 16) = make_int4((int)res[4 * c], (int)res[4 * c + 1], (int)res[4 * c + 2],
+                                                  (int)res[4 * c + 3]);
           } else {
 #pragma unroll
-            for (int b = 0; b < 16; ++b) orow[c * 16 + b] = (int8_t)(wv[b >> 2] >> (8 * (b & 3)));
+            for (int b = 0; b < DV; ++b) orow[b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
           }
         }
       }
@@ -477,6 +545,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 static thread_local std::string t_err;
 static std::atomic<uint64_t> g_launches{0};
+static std::atomic<int> g_last_grid{0};
 
 static int set_err(int code, const char* fmt, ...) {
   char buf[512];
@@ -533,11 +602,11 @@ static int sm_count(int dev) {
   return n[dev];
 }
 
-template <int DQK, int DV, bool BIAS>
+template <int DQK, int DV, bool BIAS, bool GEN>
 static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                   const CUtensorMap& mb, const KArgs& ka, cudaStream_t stream) {
   using C = Cfg<DQK, DV, BIAS>;
-  auto kern = qfa_fwd_kernel<DQK, DV, BIAS>;
+  auto kern = qfa_fwd_kernel<DQK, DV, BIAS, GEN>;
   static int per_sm[kMaxDevices] = {0};
   static std::mutex mu;
   int ctas;
@@ -546,10 +615,19 @@ static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const C
     if (per_sm[dev] == 0) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
         return set_err(QFLASH_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError()));
-      int occ = 0;
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, C::SMEM);
+      // resident CTAs per SM: registers, shared memory and TMEM columns
+      cudaFuncAttributes fa;
+      int regs = 255;
+      if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) regs = fa.numRegs;
+      int smem_sm = 0;
+      cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+      const int warp_regs = ((regs * 32 + 255) / 256) * 256;
+      const int by_regs = 65536 / (warp_regs * (kThreads / 32));
+      const int by_smem = smem_sm / (C::SMEM + 1024);
       const int by_tmem = 512 / C::TMEM_COLS;
-      int v = occ < by_tmem ? occ : by_tmem;
+      int v = by_regs < by_smem ? by_regs : by_smem;
+      v = v < by_tmem ? v : by_tmem;
+      if (const char* e = getenv("QFLASH_CTAS_PER_SM")) v = atoi(e);
       per_sm[dev] = v < 1 ? 1 : v;
     }
     ctas = per_sm[dev];
@@ -560,6 +638,7 @@ static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const C
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
+  g_last_grid.store(grid, std::memory_order_relaxed);
   return QFLASH_OK;
 }
 
@@ -681,21 +760,24 @@ extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, 
   const int passes = D == 256 ? 2 : 1;
   for (int p = 0; p < passes; ++p) {
     ka.v_col0 = p * DV;
-    if (bias) {
-      switch (D) {
-        case 32: rc = launch<32, 32, true>(dev, mq, mk, mv, mb, ka, stream); break;
-        case 64: rc = launch<64, 64, true>(dev, mq, mk, mv, mb, ka, stream); break;
-        case 128: rc = launch<128, 128, true>(dev, mq, mk, mv, mb, ka, stream); break;
-        default: rc = launch<256, 128, true>(dev, mq, mk, mv, mb, ka, stream); break;
-      }
-    } else {
-      switch (D) {
-        case 32: rc = launch<32, 32, false>(dev, mq, mk, mv, mb, ka, stream); break;
-        case 64: rc = launch<64, 64, false>(dev, mq, mk, mv, mb, ka, stream); break;
-        case 128: rc = launch<128, 128, false>(dev, mq, mk, mv, mb, ka, stream); break;
-        default: rc = launch<256, 128, false>(dev, mq, mk, mv, mb, ka, stream); break;
-      }
+    // the compact default-arithmetic kernel unless a QFLASH_* mode or the exp2
+    // range check needs the general one
+    const bool gen = (flags & (QFLASH_FLAG_EXP_IDIV | QFLASH_FLAG_L_IDIV | QFLASH_FLAG_ACC_IDIV)) ||
+                     (!bias && !ka.fast_exp);
+#define QFB_CASE(DQ, DVV)                                                                   \
+  if (bias)                                                                                 \
+    rc = gen ? launch<DQ, DVV, true, true>(dev, mq, mk, mv, mb, ka, stream)                \
+             : launch<DQ, DVV, true, false>(dev, mq, mk, mv, mb, ka, stream);              \
+  else                                                                                      \
+    rc = gen ? launch<DQ, DVV, false, true>(dev, mq, mk, mv, mb, ka, stream)               \
+             : launch<DQ, DVV, false, false>(dev, mq, mk, mv, mb, ka, stream);
+    switch (D) {
+      case 32: QFB_CASE(32, 32) break;
+      case 64: QFB_CASE(64, 64) break;
+      case 128: QFB_CASE(128, 128) break;
+      default: QFB_CASE(256, 128) break;
     }
+#undef QFB_CASE
     if (rc) return rc;
   }
   return QFLASH_OK;
@@ -714,5 +796,6 @@ extern "C" int qflash_device_error(void* stream, uint32_t* out) {
 }
 
 extern "C" uint64_t qflash_launch_count(void) { return g_launches.load(); }
+extern "C" int qflash_last_grid(void) { return g_last_grid.load(); }
 extern "C" const char* qflash_version(void) { return "qflash_b200 0.1.0 (sm_100a)"; }
 extern "C" const char* qflash_last_error(void) { return t_err.c_str(); }

@@ -56,3 +56,23 @@ def test_forward_end_to_end(golden, name):
 def test_device_error_word_clear():
     from qflash_b200 import _lib
     assert _lib.device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+TRITON_GPU = sorted(p.stem for p in (__import__("conftest").GOLDEN / "triton_gpu").glob("*.npz"))
+
+
+@pytest.mark.parametrize("name", TRITON_GPU)
+def test_div_full_matches_compiled_reference_on_b200(golden, name):
+    """QFLASH_DIV=full reproduces the reference's compiled Triton kernel on B200
+    (approximate fp32 divide), captured by tests/golden/gen_golden_triton_gpu.py."""
+    import numpy as np
+    from qflash_b200 import kernel as K
+    rec = dict(golden(name))
+    with np.load(__import__("conftest").GOLDEN / "triton_gpu" / f"{name}.npz") as z:
+        gpu = {k: z[k] for k in z.files}
+    if "bias" in gpu:
+        rec["bias"] = gpu["bias"]          # the GPU host path's bias (reciprocal-multiply rounding)
+    e, l, a, _, _ = (int(x) for x in rec["flags"])
+    o = _run_kernel(rec, flags=K.arith_flags(bool(e), bool(l), bool(a), "full"))
+    mism = int((o != gpu["o8"]).sum())
+    assert mism == 0, f"{mism} of {o.size} int8 outputs differ from the compiled reference"
