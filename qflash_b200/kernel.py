@@ -171,6 +171,23 @@ def qflash_forward(
 ):
     """Integer-only attention; same signature, arithmetic and output dtype as
     the reference's ``qflash.forward`` (qflash/kernel.py:275-351)."""
+    return forward_with_scales(query, key, value, attn_mask, scale, return_mode)
+
+
+def tensor_scales(query: Tensor, key: Tensor, value: Tensor):
+    """qflash/kernel.py:294-296: per-tensor symmetric scales amax/127, in the
+    input dtype."""
+    i8max = torch.iinfo(torch.int8).max
+    return query.abs().amax() / i8max, key.abs().amax() / i8max, value.abs().amax() / i8max
+
+
+def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mode='output',
+                        scales=None, launch=None, return_int8=False):
+    """The body of ``qflash.forward`` with two seams: ``scales`` supplies
+    (q_scale, k_scale, o_scale) computed elsewhere (the sharded path reduces
+    them over all ranks so each shard quantises exactly like the whole
+    tensor), ``launch`` replaces the kernel launch (host-logic tests), and
+    ``return_int8`` also returns (o8, o_scale)."""
     HEAD_DIM_Q, HEAD_DIM_K = query.shape[-1], key.shape[-1]
     HEAD_DIM_V = value.shape[-1]
     assert HEAD_DIM_Q == HEAD_DIM_K and HEAD_DIM_K == HEAD_DIM_V
@@ -178,12 +195,10 @@ def qflash_forward(
     if HEAD_DIM_K == 16:
         # the reference fails to compile here: tl.static_assert(BLOCK_N <= HEAD_DIM), BLOCK_N = 32
         raise ValueError("head dim 16 is not supported (the chunk width 32 exceeds it), as in the reference")
-    if not (query.is_cuda and key.is_cuda and value.is_cuda):
+    if launch is None and not (query.is_cuda and key.is_cuda and value.is_cuda):
         raise ValueError("qflash.forward runs on CUDA tensors only")
 
-    q_scale = query.abs().amax() / torch.iinfo(torch.int8).max
-    k_scale = key.abs().amax() / torch.iinfo(torch.int8).max
-    o_scale = value.abs().amax() / torch.iinfo(torch.int8).max
+    q_scale, k_scale, o_scale = tensor_scales(query, key, value) if scales is None else scales
     qk_scale = (q_scale * k_scale).item()
     sm_scale, sm_rscale, exp_M, req_M, l_M, acc_M = fixed_point_params(qk_scale, HEAD_DIM_Q, scale)
 
@@ -199,12 +214,16 @@ def qflash_forward(
     if attn_mask is not None:
         bias, bias_strides = quantize_bias(attn_mask, sm_scale, Z, H, N)
 
+    run = launch_int8 if launch is None else launch
+
     def kernel():
-        launch_int8(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides)
+        run(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides)
 
     if return_mode == 'latency':
         return do_bench(kernel, warmup=10, rep=100)
     kernel()
+    if return_int8:
+        return o * o_scale, o, o_scale
     return o * o_scale
 
 
