@@ -118,16 +118,17 @@ def cpu_sample_heads(q8, k8, v8, p, n_heads, seed=0):
 
 
 def _oracle_worker(args):
-    q, k, v, prm = args
+    q, k, v, prm, b = args
     from oracle import qflash_oracle as orc
-    return orc.attention_int8(q, k, v, prm)
+    return orc.attention_int8(q, k, v, prm, b)
 
 
-def run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs):
+def run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs, bias=None):
     """Time the oracle on the sampled heads with ``procs`` worker processes
     (spawned; each head is an independent task)."""
     from oracle import qflash_oracle as orc
-    tasks = [(q8n[z:z + 1, h:h + 1], k8n[z:z + 1, h:h + 1], v8n[z:z + 1, h:h + 1], prm) for z, h in zip(zs, hs)]
+    tasks = [(q8n[z:z + 1, h:h + 1], k8n[z:z + 1, h:h + 1], v8n[z:z + 1, h:h + 1], prm,
+              None if bias is None else bias[z:z + 1, h:h + 1]) for z, h in zip(zs, hs)]
     if procs <= 1:
         t0 = time.perf_counter()
         outs = [orc.attention_int8(*t) for t in tasks]
@@ -180,12 +181,11 @@ def main():
     dev = torch.device("cuda", local)
     # inputs: the workload's float Q/K/V, quantised by the reference host path
     q, k, v, mask = make_inputs(w, seed=a.seed + rank, device=dev)
-    if mask is not None:
-        raise SystemExit("bench.py times the unmasked workloads; masked ones are covered by the tests")
     qs, ks, vs = (t.abs().amax() / 127 for t in (q, k, v))
     sm_scale, rs, eM, rM, lM, aM = K.fixed_point_params(float((qs * ks).item()), w.D, None)
     q8, k8, v8 = K.quantize(q, qs), K.quantize(k, ks), K.quantize(v, vs)
-    del q, k, v
+    bias, bstr = (None, None) if mask is None else K.quantize_bias(mask, sm_scale, w.Z, w.H, w.N)
+    del q, k, v, mask
     # rotating input sets so that no step finds its inputs in L2 (3 x 155 MB > 126 MB)
     n_sets = 3
     sets = [(q8, k8, v8, torch.empty_like(v8))]
@@ -197,7 +197,7 @@ def main():
 
     def step(i):
         s = sets[i % n_sets]
-        K.launch_int8(s[0], s[1], s[2], s[3], rs, eM, rM, lM, aM, stream=sp)
+        K.launch_int8(s[0], s[1], s[2], s[3], rs, eM, rM, lM, aM, bias, bstr, stream=sp)
 
     for i in range(a.warmup):
         step(i)
@@ -234,7 +234,7 @@ def main():
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        K.launch_int8(dq, dk, dv, do, rs, eM, rM, lM, aM, stream=sp)
+        K.launch_int8(dq, dk, dv, do, rs, eM, rM, lM, aM, bias, bstr, stream=sp)
         ho.copy_(do, non_blocking=True)
 
     for _ in range(3):
@@ -262,25 +262,27 @@ def main():
         prm = orc.Params(sm_scale, rs, eM, rM, lM, aM)
         q8n, k8n, v8n = (t.cpu().numpy() for t in (q8, k8, v8))
         o_gpu = sets[0][3].cpu().numpy()
+        bias_n = None if bias is None else torch.as_strided(bias, (w.Z, w.H, w.N, w.N), bstr).cpu().numpy()
         zs, hs = cpu_sample_heads(q8n, k8n, v8n, prm, 2)
-        t1, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1)
+        t1, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1, bias_n)
         per_head = t1 / len(zs)
         nh = int(max(4, min(w.Z * w.H, a.cpu_seconds / max(per_head, 1e-6))))
         if world == 1:
             zs, hs = cpu_sample_heads(q8n, k8n, v8n, prm, nh, seed=1)
-            dt, outs = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1)
+            dt, outs = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1, bias_n)
             ops = 4 * len(zs) * w.N * w.N * w.D
             cpu = {"value": ops / dt / 1e12, "unit": "TOPS", "cores": 1, "kind": "port",
                    "sample": f"{len(zs)} of {w.Z * w.H} (z,h) heads of {w.name}, numpy oracle, 1 thread, {dt:.1f} s"}
             sample_exact = all(np.array_equal(o[0, 0], o_gpu[z, h]) for o, z, h in zip(outs, zs, hs))
         else:
-            dt, outs = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1)
+            dt, outs = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1, bias_n)
             sample_exact = all(np.array_equal(o[0, 0], o_gpu[z, h]) for o, z, h in zip(outs, zs, hs))
 
     ops_rank = w.ops
     value = ops_rank * world / (ms_step * 1e-3) / 1e12
     peaks, peak_src = load_peaks()
-    bytes_launch = w.io_bytes
+    bias_bytes = 0 if bias is None else int(bias.numel() * 4)
+    bytes_launch = w.io_bytes + bias_bytes
     achieved = bytes_launch / (ms_step * 1e-3) / 1e9
     traffic = profile_traffic("qfa_fwd", w.name)
     clocks = clk.summary()
@@ -303,7 +305,7 @@ def main():
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (seeded N(0,1)-family inputs of the config's shape; see qflash_b200/workloads.py)",
-        "config": {"workload": w.name, "Z": w.Z, "H": w.H, "N": w.N, "D": w.D,
+        "config": {"workload": w.name, "Z": w.Z, "H": w.H, "N": w.N, "D": w.D, "bias_bytes": bias_bytes,
                    "l2": f"{n_sets} rotating input sets ({n_sets * w.io_bytes / 1e6:.0f} MB > 126 MB L2)",
                    "parallelism": f"dp{world} (per-GPU batch fixed)", "grid_ctas": grid},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -327,21 +329,25 @@ def bench_reference(a, w, metric):
     from oracle import qflash_oracle as orc
     from qflash_b200 import kernel as K
     from qflash_b200.workloads import make_inputs
-    q, k, v, _ = make_inputs(w, seed=a.seed, device="cpu")
+    q, k, v, mask = make_inputs(w, seed=a.seed, device="cpu")
     qs, ks, vs = (t.abs().amax() / 127 for t in (q, k, v))
     sm_scale, rs, eM, rM, lM, aM = K.fixed_point_params(float((qs * ks).item()), w.D, None)
     q8n, k8n, v8n = (K.quantize(t, s).numpy() for t, s in ((q, qs), (k, ks), (v, vs)))
-    del q, k, v
+    bias_n = None
+    if mask is not None:
+        b, bstr = K.quantize_bias(mask, sm_scale, w.Z, w.H, w.N)
+        bias_n = torch.as_strided(b, (w.Z, w.H, w.N, w.N), bstr).numpy()
+    del q, k, v, mask
     prm = orc.Params(sm_scale, rs, eM, rM, lM, aM)
     procs = os.cpu_count() or 1
     # size one step to ~ a few seconds of all-core work
     zs, hs = cpu_sample_heads(q8n, k8n, v8n, prm, 2)
-    t1, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1)
+    t1, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1, bias_n)
     nh = int(max(procs, min(w.Z * w.H, 4.0 * procs / max(t1 / 2, 1e-6))))
     times = []
     for i in range(a.warmup + a.steps):
         zs, hs = cpu_sample_heads(q8n, k8n, v8n, prm, nh, seed=100 + i)
-        dt, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs)
+        dt, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs, bias_n)
         if i >= a.warmup:
             times.append(dt)
     dt = float(np.mean(times))

@@ -59,7 +59,8 @@ struct KArgs {
   long long lM, accM;
   int ls, as;                // L_SHIFT, ACC_SHIFT
   unsigned flags;
-  int fast_exp;              // host proved the 6-op exp2 form exact for this call
+  int fast_exp;              // 1: 6-op exp2 form exact for every chunk; 2: exact while the row max < m_lim
+  int m_lim;
 };
 
 // ------------------------------------------------------------------ integer primitives
@@ -160,9 +161,15 @@ struct Cfg {
   static constexpr uint32_t SWV = VA == 32 ? kSw32 : (VA == 64 ? kSw64 : kSw128);
 };
 
-// GEN = false: the reference's default arithmetic (shift forms; flags other
-// than DIV_FULL must be 0), compact code.  GEN = true: every QFLASH_* mode.
-template <int DQK, int DV, bool BIAS, bool GEN>
+// MODE selects the arithmetic the kernel is compiled for:
+//   kGen      every QFLASH_* form, chosen at run time
+//   kFast     default arithmetic, 6-op exp2 proven exact for every chunk
+//   kChecked  default arithmetic, 6-op exp2 while the row max < m_lim, else the general form
+//   kPlain    default arithmetic, general exp2 (bias kernels: the score range is unknown)
+// Flags other than DIV_FULL must be 0 for every mode but kGen.
+enum Mode : int { kGen = 0, kFast = 1, kChecked = 2, kPlain = 3 };
+
+template <int DQK, int DV, bool BIAS, int MODE>
 __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
     qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
@@ -311,11 +318,12 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
   } else {
     // ---------------------------------------------------------------- softmax warps
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    constexpr bool GEN = MODE == kGen;
     const bool exp_idiv = GEN && (a.flags & QFLASH_FLAG_EXP_IDIV);
     const bool l_idiv = GEN && (a.flags & QFLASH_FLAG_L_IDIV);
     const bool acc_idiv = GEN && (a.flags & QFLASH_FLAG_ACC_IDIV);
     const bool div_full = a.flags & QFLASH_FLAG_DIV_FULL;
-    constexpr bool kFastExp = !GEN && !BIAS;  // host guarantees the exp2_fast conditions
+
     const int rs = a.rs, eM = a.eM, rM = a.rM;
     const int S = a.as;
     // rescaling by alpha == rs is the identity while |acc| * |delta0| < 2^(S-1)
@@ -436,7 +444,9 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
           const int mx = max(max(t16[0], t16[2]), max(t16[1], t16[3]));
           const int m_new = max(m, mx);
           uint32_t pw[8];
-          if (kFastExp) {
+          bool use_fast = MODE == kFast;
+          if (MODE == kChecked) use_fast = __all_sync(0xffffffffu, m_new < a.m_lim);
+          if (use_fast) {
             const int cm1 = (int)((0u - (unsigned)m_new) * (unsigned)eM + 65536u);
             const int c3 = (int)((unsigned)rs - (unsigned)m_new);
 #pragma unroll
@@ -447,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
               const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
               pw[c] = requant_pack4(e0, e1, e2, e3, rM);
             }
-          } else {
+          } else if (MODE != kFast) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               const int e0 = exp2_generic((int)((unsigned)s[4 * c + 0] - (unsigned)m_new), rs, eM, exp_idiv);
@@ -602,11 +612,11 @@ static int sm_count(int dev) {
   return n[dev];
 }
 
-template <int DQK, int DV, bool BIAS, bool GEN>
+template <int DQK, int DV, bool BIAS, int MODE>
 static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                   const CUtensorMap& mb, const KArgs& ka, cudaStream_t stream) {
   using C = Cfg<DQK, DV, BIAS>;
-  auto kern = qfa_fwd_kernel<DQK, DV, BIAS, GEN>;
+  auto kern = qfa_fwd_kernel<DQK, DV, BIAS, MODE>;
   static int per_sm[kMaxDevices] = {0};
   static std::mutex mu;
   int ctas;
@@ -718,17 +728,28 @@ extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, 
   ka.ls = l_shift;
   ka.as = acc_shift;
   ka.flags = flags;
-  // The 6-op exp2 form (exp2_fast) is exact when no int32 value in it wraps.
-  // Without a bias a score lies in [-D*2^14, D*2^14] (int8 dot products) or is
-  // NEG_INF, the running max in [NEG_INF, D*2^14], so |x| <= xmax below; then
-  // |t1| <= |exp_M|*xmax + 2^16 and |r2| <= xmax*(|exp_M|*rs/2^16 + 1) + 2*rs.
+  // The 6-op exp2 form (exp2_fast) is exact when none of its int32 values
+  // wraps.  Without a bias a score is an int8 dot product, |s| <= D*2^14, or
+  // NEG_INF = -2^20, so with S0 = max(D*2^14, 2^20) every x = s - m_new is in
+  // [-(S0 + m_new), 0].  x*exp_M + 2^16 fits int32 for |x| <= X1 and
+  // r2 = x + (q+2)*rs fits for |x| <= X2, so rows with m_new <= min(X1, X2) - S0
+  // are safe; if that holds for the largest possible m_new (D*2^14) it always holds.
   {
-    const long long smax = (long long)D << 14;
-    const long long xmax = (smax > (1ll << 20) ? smax : (1ll << 20)) + smax;
+    const long long S0 = ((long long)D << 14) > (1ll << 20) ? ((long long)D << 14) : (1ll << 20);
     const long long aem = -(long long)exp_M;
-    const bool ok1 = aem * xmax + 65536 < (1ll << 31);
-    const bool ok2 = (xmax * (aem * sm_rscale + 65536)) / 65536 + 1 + 2ll * sm_rscale < (1ll << 31);
-    ka.fast_exp = (!bias && exp_M <= 0 && ok1 && ok2) ? 1 : 0;
+    const long long lim31 = (1ll << 31) - 1;
+    long long X = aem > 0 ? (lim31 - 65536) / aem : lim31;
+    const long long X2 = ((lim31 - 2ll * sm_rscale - 2) * 65536) / (aem * sm_rscale + 65536);
+    X = X < X2 ? X : X2;
+    const long long mlim = X - S0;
+    if (bias || exp_M > 0 || mlim <= -(1ll << 20)) {
+      ka.fast_exp = 0;
+    } else if (mlim >= ((long long)D << 14)) {
+      ka.fast_exp = 1;
+    } else {
+      ka.fast_exp = 2;
+    }
+    ka.m_lim = (int)(mlim > lim31 ? lim31 : mlim);
   }
 
   const int DV = D == 256 ? 128 : D;
@@ -760,17 +781,19 @@ extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, 
   const int passes = D == 256 ? 2 : 1;
   for (int p = 0; p < passes; ++p) {
     ka.v_col0 = p * DV;
-    // the compact default-arithmetic kernel unless a QFLASH_* mode or the exp2
-    // range check needs the general one
-    const bool gen = (flags & (QFLASH_FLAG_EXP_IDIV | QFLASH_FLAG_L_IDIV | QFLASH_FLAG_ACC_IDIV)) ||
-                     (!bias && !ka.fast_exp);
-#define QFB_CASE(DQ, DVV)                                                                   \
-  if (bias)                                                                                 \
-    rc = gen ? launch<DQ, DVV, true, true>(dev, mq, mk, mv, mb, ka, stream)                \
-             : launch<DQ, DVV, true, false>(dev, mq, mk, mv, mb, ka, stream);              \
-  else                                                                                      \
-    rc = gen ? launch<DQ, DVV, false, true>(dev, mq, mk, mv, mb, ka, stream)               \
-             : launch<DQ, DVV, false, false>(dev, mq, mk, mv, mb, ka, stream);
+    // the compact default-arithmetic kernels unless a QFLASH_* form needs the general one
+    const bool gen = flags & (QFLASH_FLAG_EXP_IDIV | QFLASH_FLAG_L_IDIV | QFLASH_FLAG_ACC_IDIV);
+    const int mode = gen ? kGen : (bias ? kPlain : (ka.fast_exp == 1 ? kFast : (ka.fast_exp == 2 ? kChecked : kGen)));
+#define QFB_CASE(DQ, DVV)                                                                           \
+  if (bias)                                                                                         \
+    rc = mode == kGen ? launch<DQ, DVV, true, kGen>(dev, mq, mk, mv, mb, ka, stream)               \
+                      : launch<DQ, DVV, true, kPlain>(dev, mq, mk, mv, mb, ka, stream);            \
+  else if (mode == kFast)                                                                           \
+    rc = launch<DQ, DVV, false, kFast>(dev, mq, mk, mv, mb, ka, stream);                            \
+  else if (mode == kChecked)                                                                        \
+    rc = launch<DQ, DVV, false, kChecked>(dev, mq, mk, mv, mb, ka, stream);                         \
+  else                                                                                              \
+    rc = launch<DQ, DVV, false, kGen>(dev, mq, mk, mv, mb, ka, stream);
     switch (D) {
       case 32: QFB_CASE(32, 32) break;
       case 64: QFB_CASE(64, 64) break;

@@ -154,6 +154,14 @@ def cases():
     D["wrap_scale40"] = ({}, lambda: (*gen(15, (1, 2, 197, 64)), None, 40.0))
     D["expm_wrap"] = ({}, lambda: (*gen(16, (1, 2, 197, 64), "outlier"), None, 2.0))
     D["tiny_scale"] = ({}, lambda: (*gen(17, (1, 2, 100, 64)), None, 0.01))
+
+    def tuned(seed, shape, kind, exp_m):
+        """inputs plus the `scale` argument that puts exp_M near -exp_m"""
+        q, k, v = gen(seed, shape, kind)
+        qk = float((q.abs().amax() / 127 * (k.abs().amax() / 127)).item())
+        return q, k, v, None, (exp_m / 65536.0) / (1.44269504 * qk)
+    D["expm_check_1100"] = ({}, lambda: tuned(31, (1, 3, 197, 64), "outlier", 1100))
+    D["expm_check_d128"] = ({}, lambda: tuned(32, (1, 2, 130, 128), "normal", 600))
     # masks
     def boolmask():
         q, k, v = gen(18, (2, 2, 70, 32))
