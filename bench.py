@@ -180,11 +180,19 @@ def main():
 
     dev = torch.device("cuda", local)
     # inputs: the workload's float Q/K/V, quantised by the reference host path
-    q, k, v, mask = make_inputs(w, seed=a.seed + rank, device=dev)
+    q, k, v, mask, win = make_inputs(w, seed=a.seed + rank, device=dev, parts=True)
     qs, ks, vs = (t.abs().amax() / 127 for t in (q, k, v))
     sm_scale, rs, eM, rM, lM, aM = K.fixed_point_params(float((qs * ks).item()), w.D, None)
     q8, k8, v8 = K.quantize(q, qs), K.quantize(k, ks), K.quantize(v, vs)
-    bias, bstr = (None, None) if mask is None else K.quantize_bias(mask, sm_scale, w.Z, w.H, w.N)
+    bias, bstr, period = None, None, 0
+    if win is not None:
+        # Swin: the bias at window granularity, as QWindowAttention / window_attention use it
+        rel, wmask = win
+        if wmask is None:
+            bias, bstr = K.quantize_bias(rel, sm_scale, w.Z, w.H, w.N)
+        else:
+            period = wmask.shape[0]
+            bias, bstr = K.quantize_bias(rel + wmask.view(period, 1, w.N, w.N), sm_scale, period, w.H, w.N)
     del q, k, v, mask
     # rotating input sets so that no step finds its inputs in L2 (3 x 155 MB > 126 MB)
     n_sets = 3
@@ -197,7 +205,7 @@ def main():
 
     def step(i):
         s = sets[i % n_sets]
-        K.launch_int8(s[0], s[1], s[2], s[3], rs, eM, rM, lM, aM, bias, bstr, stream=sp)
+        K.launch_int8(s[0], s[1], s[2], s[3], rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period)
 
     for i in range(a.warmup):
         step(i)
@@ -234,7 +242,7 @@ def main():
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        K.launch_int8(dq, dk, dv, do, rs, eM, rM, lM, aM, bias, bstr, stream=sp)
+        K.launch_int8(dq, dk, dv, do, rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period)
         ho.copy_(do, non_blocking=True)
 
     for _ in range(3):
@@ -262,7 +270,12 @@ def main():
         prm = orc.Params(sm_scale, rs, eM, rM, lM, aM)
         q8n, k8n, v8n = (t.cpu().numpy() for t in (q8, k8, v8))
         o_gpu = sets[0][3].cpu().numpy()
-        bias_n = None if bias is None else torch.as_strided(bias, (w.Z, w.H, w.N, w.N), bstr).cpu().numpy()
+        bias_n = None
+        if bias is not None:
+            zb = period or (w.Z if bstr[0] else 1)
+            bias_n = torch.as_strided(bias, (zb, w.H, w.N, w.N), bstr).cpu().numpy()
+            if period:
+                bias_n = bias_n[np.arange(w.Z) % period]
         zs, hs = cpu_sample_heads(q8n, k8n, v8n, prm, 2)
         t1, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1, bias_n)
         per_head = t1 / len(zs)
@@ -281,7 +294,7 @@ def main():
     ops_rank = w.ops
     value = ops_rank * world / (ms_step * 1e-3) / 1e12
     peaks, peak_src = load_peaks()
-    bias_bytes = 0 if bias is None else int(bias.numel() * 4)
+    bias_bytes = 0 if bias is None else int(bias.numel() * 4)   # read once per call (window granularity)
     bytes_launch = w.io_bytes + bias_bytes
     achieved = bytes_launch / (ms_step * 1e-3) / 1e9
     traffic = profile_traffic("qfa_fwd", w.name)

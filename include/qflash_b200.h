@@ -59,6 +59,21 @@ int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
                   int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
                   int32_t acc_shift, uint32_t flags, void* stream);
 
+/*
+ * qflash_i8_fwd with one more argument, bias_z_period: when > 0, batch index z
+ * reads bias batch entry z % bias_z_period (the bias then has bias_z_period
+ * entries in its batch dimension).  Swin's shifted-window bias depends on the
+ * window index only, so a [num_windows, H, N, N] bias serves a batch of
+ * num_images * num_windows windows without being expanded (the reference
+ * materialises the expanded [Z, H, N, N] bias, qflash/kernel.py:336).
+ * bias_z_period = 0 is qflash_i8_fwd.
+ */
+int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                     const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                     const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H,
+                     int N, int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
+                     int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream);
+
 /* Reads and clears the device-side error word the kernels set when a bounded
  * wait gives up (0 = none).  Synchronises the stream. */
 int qflash_device_error(void* stream, uint32_t* out);

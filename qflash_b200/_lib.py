@@ -29,6 +29,12 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p]),
+    "qflash_i8_fwd_ex": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        _I64x4, _I64x4, _I64x4, _I64x4, _I64x4, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p]),
     "qflash_device_error": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "qflash_launch_count": (ctypes.c_uint64, []),
     "qflash_last_grid": (ctypes.c_int, []),
@@ -72,15 +78,15 @@ def _check(rc: int, what: str):
 
 
 def i8_fwd(q, k, v, o, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
-           l_shift, acc_shift, flags, stream) -> None:
+           l_shift, acc_shift, flags, stream, bias_z_period=0) -> None:
     """Launch the attention kernel on device tensors (no synchronisation)."""
     lib = load()
     bs = (ctypes.c_int64 * 4)(*bias_strides) if bias is not None else None
-    rc = lib.qflash_i8_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                           bias.data_ptr() if bias is not None else None,
-                           _strides(q), _strides(k), _strides(v), _strides(o), bs,
-                           Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags, stream)
-    _check(rc, "qflash_i8_fwd")
+    rc = lib.qflash_i8_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                              bias.data_ptr() if bias is not None else None,
+                              _strides(q), _strides(k), _strides(v), _strides(o), bs, bias_z_period,
+                              Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags, stream)
+    _check(rc, "qflash_i8_fwd_ex")
 
 
 def device_error(stream) -> int:

@@ -11,7 +11,7 @@ from typing import Dict, Optional
 import torch
 from torch import nn
 
-from .kernel import qflash
+from .kernel import qflash, window_attention
 from .swin import relative_position_index
 
 try:  # pragma: no cover - exercised only where timm is installed
@@ -88,13 +88,10 @@ class QWindowAttention(nn.Module):
         qkv = self.qkv(x).reshape(B_, N, 3, self.num_heads, -1).permute(2, 0, 3, 1, 4)
         q, k, v = qkv.unbind(0)
 
-        attn_mask = self._get_rel_pos_bias()
-        if mask is not None:
-            num_win = mask.shape[0]
-            mask = mask.view(1, num_win, 1, N, N).expand(B_ // num_win, -1, self.num_heads, -1, -1)
-            attn_mask = attn_mask + mask.reshape(-1, self.num_heads, N, N)
-
-        x = qflash.forward(q, k, v, attn_mask=attn_mask)
+        # the reference adds the (window) mask to the bias at full batch size and
+        # calls qflash.forward(q, k, v, attn_mask=...); window_attention gives the
+        # same result from the per-window bias (see its docstring)
+        x = window_attention(q, k, v, self._get_rel_pos_bias(), mask)
         return self.proj(x.transpose(1, 2).reshape(B_, N, -1))
 
     @classmethod

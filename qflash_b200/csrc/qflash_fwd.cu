@@ -49,8 +49,9 @@ enum : unsigned { kErrQEmpty = 1, kErrKvEmpty = 2, kErrQFull = 4, kErrKvFull = 8
                   kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128 };
 
 struct KArgs {
-  int Z, H, N, nch, ntiles, nitems;
+  int Z, H, N, nch, ntiles, nitems, ZH;
   int bias_hb, bias_zb;      // 1 if the bias has a real H / Z dimension, 0 if broadcast
+  int bias_zmod;             // > 0: the bias batch index is z mod bias_zmod (Swin window period)
   int v_col0;                // first output column handled (head dim 256 runs as two halves)
   int8_t* o;
   long long os_z, os_h, os_n;
@@ -136,15 +137,20 @@ __device__ __forceinline__ int div_to_i32(int acc, int l, bool full) {
 }
 
 // ------------------------------------------------------------------ kernel
-template <int DQK, int DV, bool BIAS>
+// SEGS = 2 packs two heads (of N <= 64 rows each) into one 128-row tile:
+// rows [0, 64) belong to head 2*item, rows [64, 128) to head 2*item + 1.
+template <int DQK, int DV, bool BIAS, int SEGS>
 struct Cfg {
+  static constexpr int SEG_ROWS = kBM / SEGS;
   static constexpr int QA = DQK < 128 ? DQK : 128;  // bytes per row of one swizzle atom
   static constexpr int NQA = DQK / QA;              // atoms along the QK contraction
   static constexpr int VA = DV;                     // DV <= 128: one atom
   static constexpr int KVS = BIAS ? 4 : 8;          // K/V chunk stages
   static constexpr int Q_BYTES = kBM * DQK;
-  static constexpr int K_BYTES = kBN * DQK;
-  static constexpr int V_BYTES = kBN * DV;
+  static constexpr int K_SEG = kBN * DQK;
+  static constexpr int V_SEG = kBN * DV;
+  static constexpr int K_BYTES = SEGS * K_SEG;
+  static constexpr int V_BYTES = SEGS * V_SEG;
   static constexpr int B_BYTES = BIAS ? kBM * kBN * 4 : 0;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
@@ -154,7 +160,11 @@ struct Cfg {
   static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
-  static constexpr int TMEM_COLS = (64 + 2 * DV) <= 128 ? 128 : ((64 + 2 * DV) <= 256 ? 256 : 512);
+  static constexpr int S_COLS = 32 * SEGS;           // one S slot: a 32-column region per segment
+  static constexpr int PV_OFF = 2 * S_COLS;          // TMEM column of PV slot 0
+  static constexpr int PV_SLOT = SEGS * DV;
+  static constexpr int TMEM_NEED = PV_OFF + 2 * PV_SLOT;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512);
   static constexpr uint32_t IDESC_S = idesc_i8(kBM, kBN, false);
   static constexpr uint32_t IDESC_PV = idesc_i8(kBM, DV, true);
   static constexpr uint32_t SWQ = QA == 32 ? kSw32 : (QA == 64 ? kSw64 : kSw128);
@@ -169,12 +179,12 @@ struct Cfg {
 // Flags other than DIV_FULL must be 0 for every mode but kGen.
 enum Mode : int { kGen = 0, kFast = 1, kChecked = 2, kPlain = 3 };
 
-template <int DQK, int DV, bool BIAS, int MODE>
+template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
 __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
     qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
                    const KArgs a) {
-  using C = Cfg<DQK, DV, BIAS>;
+  using C = Cfg<DQK, DV, BIAS, SEGS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
@@ -236,6 +246,20 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
   };
 
   const int nch = a.nch;
+  // head (z, h) and first query row of segment `sg` of work item `item`; false if the segment is empty
+  auto decode = [&](int item, int sg, int& z, int& h, int& row0) -> bool {
+    int zh;
+    if (SEGS == 1) {
+      zh = item / a.ntiles;
+      row0 = (item - zh * a.ntiles) * kBM;
+    } else {
+      zh = item * SEGS + sg;
+      row0 = 0;
+    }
+    z = zh / a.H;
+    h = zh - z * a.H;
+    return zh < a.ZH;
+  };
 
   if (warp == 4) {
     // ---------------------------------------------------------------- TMA producer
@@ -248,27 +272,39 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       int qi = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x, ++qi) {
-        const int zh = item / a.ntiles, tile = item - zh * a.ntiles;
-        const int z = zh / a.H, h = zh - z * a.H;
+        int nseg = 0;
+        for (int sg = 0; sg < SEGS; ++sg) {
+          int z, h, r0;
+          nseg += decode(item, sg, z, h, r0) ? 1 : 0;
+        }
         const int qb = qi & 1;
         if (!(ok = wait(q_empty(qb), ((qi >> 1) & 1) ^ 1, kErrQEmpty))) break;
-        mbar_arrive_expect_tx(q_full(qb), C::Q_BYTES);
+        mbar_arrive_expect_tx(q_full(qb), nseg * C::SEG_ROWS * DQK);
+        for (int sg = 0; sg < SEGS; ++sg) {
+          int z, h, r0;
+          if (!decode(item, sg, z, h, r0)) continue;
 #pragma unroll
-        for (int at = 0; at < C::NQA; ++at)
-          tma_load_4d(sbase + C::OFF_Q + qb * C::Q_BYTES + at * kBM * C::QA, &tmQ, q_full(qb), at * C::QA,
-                      tile * kBM, h, z);
+          for (int at = 0; at < C::NQA; ++at)
+            tma_load_4d(sbase + C::OFF_Q + qb * C::Q_BYTES + at * kBM * C::QA + sg * C::SEG_ROWS * C::QA, &tmQ,
+                        q_full(qb), at * C::QA, r0, h, z);
+        }
         for (int j = 0; j < nch; ++j, ++kv_it) {
           const int st = kv_it % C::KVS;
           if (!(ok = wait(kv_empty(st), ((kv_it / C::KVS) & 1) ^ 1, kErrKvEmpty))) break;
-          mbar_arrive_expect_tx(kv_full(st), C::K_BYTES + C::V_BYTES + C::B_BYTES);
+          mbar_arrive_expect_tx(kv_full(st), nseg * (C::K_SEG + C::V_SEG + C::B_BYTES / SEGS));
+          for (int sg = 0; sg < SEGS; ++sg) {
+            int z, h, r0;
+            if (!decode(item, sg, z, h, r0)) continue;
 #pragma unroll
-          for (int at = 0; at < C::NQA; ++at)
-            tma_load_4d(sbase + C::OFF_K + st * C::K_BYTES + at * kBN * C::QA, &tmK, kv_full(st), at * C::QA,
-                        j * kBN, h, z);
-          tma_load_4d(sbase + C::OFF_V + st * C::V_BYTES, &tmV, kv_full(st), a.v_col0, j * kBN, h, z);
-          if (BIAS)
-            tma_load_4d(sbase + C::OFF_B + st * C::B_BYTES, &tmB, kv_full(st), j * kBN, tile * kBM,
-                        a.bias_hb ? h : 0, a.bias_zb ? z : 0);
+            for (int at = 0; at < C::NQA; ++at)
+              tma_load_4d(sbase + C::OFF_K + st * C::K_BYTES + sg * C::K_SEG + at * kBN * C::QA, &tmK, kv_full(st),
+                          at * C::QA, j * kBN, h, z);
+            tma_load_4d(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, &tmV, kv_full(st), a.v_col0, j * kBN,
+                        h, z);
+            if (BIAS)
+              tma_load_4d(sbase + C::OFF_B + st * C::B_BYTES + sg * C::SEG_ROWS * 128, &tmB, kv_full(st), j * kBN,
+                          r0, a.bias_hb ? h : 0, a.bias_zb ? (a.bias_zmod ? z % a.bias_zmod : z) : 0);
+          }
         }
       }
     }
@@ -284,8 +320,12 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
         if (!wait(p_full(slot), (gg >> 1) & 1, kErrPFull)) return false;
         if (!wait(pv_empty(slot), ((gg >> 1) & 1) ^ 1, kErrPvEmpty)) return false;
         tc_fence_after();
-        const uint64_t bdesc = smem_desc(sbase + C::OFF_V + st * C::V_BYTES, kBN * C::VA, 8 * C::VA, C::SWV);
-        mma_i8_ts(tmem + 64 + slot * DV, tmem + slot * 32, bdesc, C::IDESC_PV, 0);
+#pragma unroll
+        for (int sg = 0; sg < SEGS; ++sg) {
+          const uint64_t bdesc =
+              smem_desc(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, kBN * C::VA, 8 * C::VA, C::SWV);
+          mma_i8_ts(tmem + C::PV_OFF + slot * C::PV_SLOT + sg * DV, tmem + slot * C::S_COLS, bdesc, C::IDESC_PV, 0);
+        }
         tc_commit(pv_full(slot));
         tc_commit(kv_empty(st));
         return true;
@@ -300,13 +340,16 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
           if (!(ok = wait(kv_full(st), (g / C::KVS) & 1, kErrKvFull))) break;
           tc_fence_after();
           const uint32_t kaddr = sbase + C::OFF_K + st * C::K_BYTES;
-          const uint32_t dS = tmem + (g & 1) * 32;
 #pragma unroll
-          for (int kk = 0; kk < DQK / 32; ++kk) {
-            const int at = (kk * 32) / C::QA, off = (kk * 32) % C::QA;
-            const uint64_t ad = smem_desc(qaddr + at * kBM * C::QA + off, 16, 8 * C::QA, C::SWQ);
-            const uint64_t bd = smem_desc(kaddr + at * kBN * C::QA + off, 16, 8 * C::QA, C::SWQ);
-            mma_i8_ss(dS, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+          for (int sg = 0; sg < SEGS; ++sg) {
+            const uint32_t dS = tmem + (g & 1) * C::S_COLS + sg * 32;
+#pragma unroll
+            for (int kk = 0; kk < DQK / 32; ++kk) {
+              const int at = (kk * 32) / C::QA, off = (kk * 32) % C::QA;
+              const uint64_t ad = smem_desc(qaddr + at * kBM * C::QA + off, 16, 8 * C::QA, C::SWQ);
+              const uint64_t bd = smem_desc(kaddr + sg * C::K_SEG + at * kBN * C::QA + off, 16, 8 * C::QA, C::SWQ);
+              mma_i8_ss(dS, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+            }
           }
           tc_commit(s_full(g & 1));
           if (j == nch - 1) tc_commit(q_empty(qb));
@@ -333,9 +376,12 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
     uint32_t g = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x) {
-      const int zh = item / a.ntiles, tile = item - zh * a.ntiles;
-      const int row0 = tile * kBM + warp * 32;
-      const bool active = row0 < a.N;
+      // warp -> segment (head) and its 32-row slice
+      const int sg = SEGS == 1 ? 0 : warp / (4 / SEGS);
+      int z, h, rbase;
+      const bool seg_ok = decode(item, sg, z, h, rbase);
+      const int row0 = rbase + (SEGS == 1 ? warp : warp % (4 / SEGS)) * 32;
+      const bool active = seg_ok && row0 < a.N;
       const int row = row0 + lane;
       const bool row_ok = row < a.N;
       int m = kNegInf, l = 1, alpha_prev = 0;
@@ -356,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
           const bool skip = first || __all_sync(0xffffffffu, ident || !row_ok);
           const bool fast = !acc_idiv && S < 32 && A >= 0 && A < (1ll << 32);
           const int mode = skip ? 0 : (__all_sync(0xffffffffu, fast) ? 1 : 2);
-          const uint32_t base = tmem + lane_base + 64 + slot * DV;
+          const uint32_t base = tmem + lane_base + C::PV_OFF + slot * C::PV_SLOT + sg * DV;
           if (mode == 0) {
 #pragma unroll
             for (int part = 0; part < DV / 32; ++part) {
@@ -416,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
         int alpha = 0;
         if (active) {
           int s[32];
-          tmem_ld32(tmem + lane_base + slot * 32, s);
+          tmem_ld32(tmem + lane_base + slot * C::S_COLS + sg * 32, s);
           if (BIAS) {
             const uint8_t* brow = smem + C::OFF_B + (g % C::KVS) * C::B_BYTES + (warp * 32 + lane) * 128;
 #pragma unroll
@@ -468,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
             }
           }
           alpha = exp2_generic((int)((unsigned)m - (unsigned)m_new), rs, eM, exp_idiv);
-          tmem_st8(tmem + lane_base + slot * 32, pw);
+          tmem_st8(tmem + lane_base + slot * C::S_COLS, pw);
           // l_j = sum of the 32 int8 P values, two independent dot-product chains
           int ls0 = 0, ls1 = 0;
 #pragma unroll
@@ -492,7 +538,6 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
 
       // epilogue: O row = int8(int32(fp32(acc) / fp32(l)))
       if (active) {
-        const int z = zh / a.H, h = zh - z * a.H;
         int8_t* orow = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row * a.os_n + a.v_col0;
         // Exact shortcut: for |acc| < 2^23 and 0 < l < 2^24, trunc(RN_f32(acc / l))
         // equals the truncated integer quotient (rounding up to an integer n >= 2
@@ -612,11 +657,11 @@ static int sm_count(int dev) {
   return n[dev];
 }
 
-template <int DQK, int DV, bool BIAS, int MODE>
+template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
 static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                   const CUtensorMap& mb, const KArgs& ka, cudaStream_t stream) {
-  using C = Cfg<DQK, DV, BIAS>;
-  auto kern = qfa_fwd_kernel<DQK, DV, BIAS, MODE>;
+  using C = Cfg<DQK, DV, BIAS, SEGS>;
+  auto kern = qfa_fwd_kernel<DQK, DV, BIAS, MODE, SEGS>;
   static int per_sm[kMaxDevices] = {0};
   static std::mutex mu;
   int ctas;
@@ -685,11 +730,11 @@ static int select_device(const void* p, int* dev) {
 
 using namespace qfb;
 
-extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
-                             const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
-                             const int64_t o_strides[4], const int64_t bias_strides[4], int Z, int H, int N, int D,
-                             int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
-                             int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream_) {
+extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                                const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                                const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z,
+                                int H, int N, int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M,
+                                int64_t acc_M, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream_) {
   cudaStream_t stream = (cudaStream_t)stream_;
   if (Z < 0 || H < 0 || N < 0) return set_err(QFLASH_ERR_ARG, "negative shape");
   if (!(D == 32 || D == 64 || D == 128 || D == 256)) return set_err(QFLASH_ERR_ARG, "head dim %d not in {32,64,128,256}", D);
@@ -710,8 +755,15 @@ extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, 
   ka.H = H;
   ka.N = N;
   ka.nch = (N + kBN - 1) / kBN;
-  ka.ntiles = (N + kBM - 1) / kBM;
-  const long long items = (long long)Z * H * ka.ntiles;
+  // two heads per 128-row tile when a head has at most 64 query rows
+  const int segs = (N <= kBM / 2 && (D == 32 || D == 64)) ? 2 : 1;
+  ka.ntiles = segs == 2 ? 1 : (N + kBM - 1) / kBM;
+  const long long zh_total = (long long)Z * H;
+  if (zh_total > 0x7fffffffLL) return set_err(QFLASH_ERR_ARG, "too many heads");
+  ka.ZH = (int)zh_total;
+  const long long items = segs == 2 ? (zh_total + 1) / 2 : zh_total * ka.ntiles;
+  if (bias_z_period < 0) return set_err(QFLASH_ERR_ARG, "negative bias_z_period");
+  ka.bias_zmod = bias_z_period;
   if (items > 0x7fffffffLL) return set_err(QFLASH_ERR_ARG, "too many tiles");
   ka.nitems = (int)items;
   ka.o = o;
@@ -758,7 +810,7 @@ extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, 
   memset(&mb, 0, sizeof(mb));
   int rc;
   if ((rc = make_map(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, D, N, H, Z, q_strides[2], q_strides[1], q_strides[0], qa,
-                     kBM, qa)))
+                     kBM / segs, qa)))
     return rc;
   if ((rc = make_map(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, D, N, H, Z, k_strides[2], k_strides[1], k_strides[0], qa,
                      kBN, qa)))
@@ -771,11 +823,13 @@ extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, 
     if (bc != 1) return set_err(QFLASH_ERR_ARG, "bias innermost stride must be 1");
     ka.bias_zb = bz != 0;
     ka.bias_hb = bh != 0;
+    if (bias_z_period > 0 && !bz) return set_err(QFLASH_ERR_ARG, "bias_z_period needs a batch dimension in the bias");
+    const int zb = bz ? (bias_z_period > 0 ? bias_z_period : Z) : 1;
     const uint64_t row_b = (uint64_t)br * 4;
     const uint64_t h_b = bh ? (uint64_t)bh * 4 : row_b * N;
     const uint64_t z_b = bz ? (uint64_t)bz * 4 : h_b * (bh ? H : 1);
-    if ((rc = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_INT32, bias, N, N, bh ? H : 1, bz ? Z : 1, row_b, h_b, z_b, kBN,
-                       kBM, 128)))
+    if ((rc = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_INT32, bias, N, N, bh ? H : 1, zb, row_b, h_b, z_b, kBN,
+                       kBM / segs, 128)))
       return rc;
   }
   const int passes = D == 256 ? 2 : 1;
@@ -784,26 +838,39 @@ extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, 
     // the compact default-arithmetic kernels unless a QFLASH_* form needs the general one
     const bool gen = flags & (QFLASH_FLAG_EXP_IDIV | QFLASH_FLAG_L_IDIV | QFLASH_FLAG_ACC_IDIV);
     const int mode = gen ? kGen : (bias ? kPlain : (ka.fast_exp == 1 ? kFast : (ka.fast_exp == 2 ? kChecked : kGen)));
-#define QFB_CASE(DQ, DVV)                                                                           \
-  if (bias)                                                                                         \
-    rc = mode == kGen ? launch<DQ, DVV, true, kGen>(dev, mq, mk, mv, mb, ka, stream)               \
-                      : launch<DQ, DVV, true, kPlain>(dev, mq, mk, mv, mb, ka, stream);            \
-  else if (mode == kFast)                                                                           \
-    rc = launch<DQ, DVV, false, kFast>(dev, mq, mk, mv, mb, ka, stream);                            \
-  else if (mode == kChecked)                                                                        \
-    rc = launch<DQ, DVV, false, kChecked>(dev, mq, mk, mv, mb, ka, stream);                         \
-  else                                                                                              \
-    rc = launch<DQ, DVV, false, kGen>(dev, mq, mk, mv, mb, ka, stream);
+#define QFB_LAUNCH(DQ, DVV, B, M) \
+  (segs == 2 ? launch<DQ, DVV, B, M, 2>(dev, mq, mk, mv, mb, ka, stream) : launch<DQ, DVV, B, M, 1>(dev, mq, mk, mv, mb, ka, stream))
+#define QFB_LAUNCH1(DQ, DVV, B, M) launch<DQ, DVV, B, M, 1>(dev, mq, mk, mv, mb, ka, stream)
+#define QFB_CASE(DQ, DVV, L)                                                      \
+  if (bias)                                                                       \
+    rc = mode == kGen ? L(DQ, DVV, true, kGen) : L(DQ, DVV, true, kPlain);        \
+  else if (mode == kFast)                                                         \
+    rc = L(DQ, DVV, false, kFast);                                                \
+  else if (mode == kChecked)                                                      \
+    rc = L(DQ, DVV, false, kChecked);                                             \
+  else                                                                            \
+    rc = L(DQ, DVV, false, kGen);
     switch (D) {
-      case 32: QFB_CASE(32, 32) break;
-      case 64: QFB_CASE(64, 64) break;
-      case 128: QFB_CASE(128, 128) break;
-      default: QFB_CASE(256, 128) break;
+      case 32: QFB_CASE(32, 32, QFB_LAUNCH) break;
+      case 64: QFB_CASE(64, 64, QFB_LAUNCH) break;
+      case 128: QFB_CASE(128, 128, QFB_LAUNCH1) break;
+      default: QFB_CASE(256, 128, QFB_LAUNCH1) break;
     }
+#undef QFB_LAUNCH
+#undef QFB_LAUNCH1
 #undef QFB_CASE
     if (rc) return rc;
   }
   return QFLASH_OK;
+}
+
+extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                             const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                             const int64_t o_strides[4], const int64_t bias_strides[4], int Z, int H, int N, int D,
+                             int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
+                             int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream) {
+  return qflash_i8_fwd_ex(q, k, v, o, bias, q_strides, k_strides, v_strides, o_strides, bias_strides, 0, Z, H, N, D,
+                          sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags, stream);
 }
 
 extern "C" int qflash_device_error(void* stream, uint32_t* out) {

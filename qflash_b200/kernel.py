@@ -144,7 +144,8 @@ def do_bench(fn, warmup: float = 10, rep: float = 100) -> float:
 
 def launch_int8(q8: Tensor, k8: Tensor, v8: Tensor, o8: Tensor, sm_rscale: int, exp_M: int, req_M: int,
                 l_M: int, acc_M: int, bias: Tensor | None = None, bias_strides=None,
-                l_shift: int = None, acc_shift: int = None, flags: int = None, stream=None) -> None:
+                l_shift: int = None, acc_shift: int = None, flags: int = None, stream=None,
+                bias_z_period: int = 0) -> None:
     """Run the sm_100a kernel on int8 [Z, H, N, D] tensors already on the GPU
     (the launch at qflash/kernel.py:319-326 / 339-346)."""
     for t in (q8, k8, v8, o8):
@@ -158,7 +159,7 @@ def launch_int8(q8: Tensor, k8: Tensor, v8: Tensor, o8: Tensor, sm_rscale: int, 
             raise OverflowError(f"{name}={val} does not fit in int32")
     _lib.i8_fwd(q8, k8, v8, o8, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
                 L_SHIFT if l_shift is None else l_shift, ACC_SHIFT if acc_shift is None else acc_shift,
-                arith_flags() if flags is None else flags, stream)
+                arith_flags() if flags is None else flags, stream, bias_z_period)
 
 
 def qflash_forward(
@@ -182,12 +183,14 @@ def tensor_scales(query: Tensor, key: Tensor, value: Tensor):
 
 
 def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mode='output',
-                        scales=None, launch=None, return_int8=False):
+                        scales=None, launch=None, return_int8=False, bias_z_period=0):
     """The body of ``qflash.forward`` with two seams: ``scales`` supplies
     (q_scale, k_scale, o_scale) computed elsewhere (the sharded path reduces
     them over all ranks so each shard quantises exactly like the whole
     tensor), ``launch`` replaces the kernel launch (host-logic tests), and
-    ``return_int8`` also returns (o8, o_scale)."""
+    ``return_int8`` also returns (o8, o_scale); ``bias_z_period`` > 0 means
+    ``attn_mask`` has that many batch entries and batch z uses entry
+    z % bias_z_period (see ``window_attention``)."""
     HEAD_DIM_Q, HEAD_DIM_K = query.shape[-1], key.shape[-1]
     HEAD_DIM_V = value.shape[-1]
     assert HEAD_DIM_Q == HEAD_DIM_K and HEAD_DIM_K == HEAD_DIM_V
@@ -212,12 +215,14 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
     Z, H, N = query.shape[0], query.shape[1], query.shape[2]
     bias, bias_strides = None, None
     if attn_mask is not None:
-        bias, bias_strides = quantize_bias(attn_mask, sm_scale, Z, H, N)
-
-    run = launch_int8 if launch is None else launch
+        bias, bias_strides = quantize_bias(attn_mask, sm_scale, bias_z_period or Z, H, N)
 
     def kernel():
-        run(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides)
+        if launch is not None:
+            launch(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides)
+        else:
+            launch_int8(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides,
+                        bias_z_period=bias_z_period)
 
     if return_mode == 'latency':
         return do_bench(kernel, warmup=10, rep=100)
@@ -225,6 +230,29 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
     if return_int8:
         return o * o_scale, o, o_scale
     return o * o_scale
+
+
+def window_attention(query, key, value, rel_bias, window_mask=None, scale=None, return_mode='output'):
+    """Swin window attention with the bias kept at window granularity.
+
+    Equals ``qflash_forward(query, key, value, attn_mask=rel_bias + mask)``
+    with the [B_, H, N, N] float mask that QWindowAttention builds
+    (qflash/attention.py:72-76) -- bit for bit, because that mask's entry
+    (b, h) is rel_bias[h] + window_mask[b % nW] and the bias quantisation is
+    elementwise.  Here the sum and its quantisation are formed once per
+    (window, head), [nW, H, N, N], and the kernel reads entry b % nW, so
+    neither the expanded float mask nor the expanded int32 bias is built.
+
+    query/key/value: [B_, H, N, D] with B_ a multiple of nW; rel_bias:
+    [1, H, N, N]; window_mask: [nW, N, N] (0 / -100 shifted-window mask) or None.
+    """
+    if window_mask is None:
+        return forward_with_scales(query, key, value, rel_bias, scale, return_mode)
+    nW, N = window_mask.shape[0], window_mask.shape[-1]
+    if query.shape[0] % nW:
+        raise ValueError(f"batch {query.shape[0]} is not a multiple of the {nW} windows")
+    attn_mask = rel_bias + window_mask.view(nW, 1, N, N)
+    return forward_with_scales(query, key, value, attn_mask, scale, return_mode, bias_z_period=nW)
 
 
 class qflash:

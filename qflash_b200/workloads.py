@@ -11,7 +11,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .swin import relative_position_index, shifted_window_mask, window_attn_mask
+from .swin import relative_position_index, shifted_window_mask, window_attn_mask, window_bias
 
 
 @dataclass(frozen=True)
@@ -58,10 +58,12 @@ def _normal(shape, g, device, dtype):
     return torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(dtype)
 
 
-def make_inputs(w: Workload, seed: int = 0, device="cpu", dtype=torch.float32):
+def make_inputs(w: Workload, seed: int = 0, device="cpu", dtype=torch.float32, parts: bool = False):
     """Return (q, k, v, attn_mask) for workload ``w``; attn_mask is None
     except for Swin, where it is the float bias(+shift mask) tensor that
-    QWindowAttention passes to ``qflash.forward``."""
+    QWindowAttention builds at full batch size.  With ``parts`` a fifth item
+    (rel_bias [1, H, N, N], window_mask [nW, N, N] or None) is appended (None
+    for non-Swin workloads)."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     shape = (w.Z, w.H, w.N, w.D)
@@ -83,6 +85,7 @@ def make_inputs(w: Workload, seed: int = 0, device="cpu", dtype=torch.float32):
     else:
         raise ValueError(w.dist)
     attn_mask = None
+    win_parts = None
     if w.dist == "swin":
         win = 7
         table = torch.randn(((2 * win - 1) ** 2, w.H), generator=g, device=device) * 0.02
@@ -92,4 +95,6 @@ def make_inputs(w: Workload, seed: int = 0, device="cpu", dtype=torch.float32):
             side = int(round(w.windows ** 0.5)) * win
             mask = shifted_window_mask(side, side, win, win // 2).to(device)
         attn_mask = window_attn_mask(table, index, w.images, mask)
-    return q.to(dtype), k.to(dtype), v.to(dtype), attn_mask
+        win_parts = (window_bias(table, index), mask)
+    out = (q.to(dtype), k.to(dtype), v.to(dtype), attn_mask)
+    return out + (win_parts,) if parts else out
