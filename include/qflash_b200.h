@@ -11,6 +11,7 @@
 #ifndef QFLASH_B200_H_
 #define QFLASH_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -73,6 +74,42 @@ int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* 
                      const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H,
                      int N, int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
                      int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream);
+
+/*
+ * The whole forward of qflash.forward on the device, without the reference's
+ * host synchronisation (the `.item()` at qflash/kernel.py:297): per-tensor
+ * scales (kernel.py:294-296), the fixed-point constants (kernel.py:298-307,
+ * Python double arithmetic), int8 quantisation (kernel.py:309-311), bias
+ * quantisation (kernel.py:328-336), the attention kernel and the dequantised
+ * output o * o_scale (kernel.py:351) -- each step as torch evaluates it on a
+ * CUDA device, so the output equals the reference's bit for bit.
+ *   q, k, v        float [Z, H, N, D], dtype 0 = f32, 1 = f16, 2 = bf16; strides in
+ *                  elements with the head dim contiguous
+ *   mask           optional additive float mask (mask_dtype 0/1/2) or bool mask (3),
+ *                  broadcast to [Z, H, N, N] through mask_strides (0 on broadcast
+ *                  dims); mask_zb / mask_hb its batch / head extents (1, Z or
+ *                  mask_z_period; 1 or H); mask_z_period as in qflash_i8_fwd_ex
+ *   q8, k8, v8, o8 int8 [Z, H, N, D] contiguous: the quantised tensors and the int8 output
+ *   out            [Z, H, N, D] contiguous, dtype of q (all NaN if the constants
+ *                  cannot be formed -- where the reference raises, e.g. q or k all zero)
+ *   scale_log2e    the softmax scale times 1.44269504 (kernel.py:290-292)
+ *   workspace      device memory, 256-byte aligned, >= qflash_fused_workspace_bytes()
+ * Asynchronous on `stream`; qflash_fused_status() reports the constants' status.
+ */
+int qflash_fwd_fused(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
+                     const int64_t k_strides[4], const int64_t v_strides[4], const void* mask, int mask_dtype,
+                     const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period, int8_t* q8,
+                     int8_t* k8, int8_t* v8, int8_t* o8, void* out, int Z, int H, int N, int D, double scale_log2e,
+                     int32_t l_shift, int32_t acc_shift, uint32_t flags, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Workspace bytes qflash_fwd_fused needs (mask_zb = mask_hb = 0 without a mask). */
+size_t qflash_fused_workspace_bytes(int mask_zb, int mask_hb, int N);
+
+/* Synchronises the stream and reads the status the fused forward recorded in its
+ * workspace: 0 ok, 1 division by zero (the reference raises ZeroDivisionError),
+ * 2 constants not representable (NaN/inf scales, or beyond int32). */
+int qflash_fused_status(const void* workspace, void* stream, int64_t* status);
 
 /* Reads and clears the device-side error word the kernels set when a bounded
  * wait gives up (0 = none).  Synchronises the stream. */

@@ -35,6 +35,14 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p]),
+    "qflash_fwd_fused": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, _I64x4, _I64x4, _I64x4,
+        ctypes.c_void_p, ctypes.c_int, _I64x4, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "qflash_fused_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qflash_fused_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)]),
     "qflash_device_error": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "qflash_launch_count": (ctypes.c_uint64, []),
     "qflash_last_grid": (ctypes.c_int, []),
@@ -87,6 +95,35 @@ def i8_fwd(q, k, v, o, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, 
                               _strides(q), _strides(k), _strides(v), _strides(o), bs, bias_z_period,
                               Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags, stream)
     _check(rc, "qflash_i8_fwd_ex")
+
+
+DTYPES = {"torch.float32": 0, "torch.float16": 1, "torch.bfloat16": 2, "torch.bool": 3}
+
+
+def fwd_fused(q, k, v, mask, mask_strides, mask_zb, mask_hb, mask_z_period, q8, k8, v8, o8, out,
+              scale_log2e, l_shift, acc_shift, flags, workspace, stream) -> None:
+    """Launch the on-device forward (qflash_fwd_fused); no synchronisation."""
+    lib = load()
+    Z, H, N, D = q.shape
+    ms = (ctypes.c_int64 * 4)(*mask_strides) if mask is not None else None
+    rc = lib.qflash_fwd_fused(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPES[str(q.dtype)],
+                              _strides(q), _strides(k), _strides(v),
+                              mask.data_ptr() if mask is not None else None,
+                              DTYPES[str(mask.dtype)] if mask is not None else -1, ms, mask_zb, mask_hb, mask_z_period,
+                              q8.data_ptr(), k8.data_ptr(), v8.data_ptr(), o8.data_ptr(), out.data_ptr(),
+                              Z, H, N, D, scale_log2e, l_shift, acc_shift, flags,
+                              workspace.data_ptr(), workspace.numel(), stream)
+    _check(rc, "qflash_fwd_fused")
+
+
+def fused_workspace_bytes(mask_zb: int, mask_hb: int, N: int) -> int:
+    return int(load().qflash_fused_workspace_bytes(mask_zb, mask_hb, N))
+
+
+def fused_status(workspace, stream) -> int:
+    out = ctypes.c_int64(0)
+    _check(load().qflash_fused_status(workspace.data_ptr(), stream, ctypes.byref(out)), "qflash_fused_status")
+    return int(out.value)
 
 
 def device_error(stream) -> int:

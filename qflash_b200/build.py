@@ -2,8 +2,9 @@
 
     python -m qflash_b200.build [--force]
 
-nvcc compiles ``csrc/qflash_fwd.cu`` straight to a shared library (cudart
-linked statically); nothing else is needed at run time besides the driver.
+nvcc compiles each ``csrc/*.cu`` to an object under ``_build/`` and links
+the shared library (cudart linked statically); nothing else is needed at run
+time besides the driver.
 """
 from __future__ import annotations
 
@@ -17,10 +18,10 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libqflash_b200.so"
-SOURCES = [CSRC / "qflash_fwd.cu"]
-HEADERS = [CSRC / "sm100_ptx.cuh", PKG.parent / "include" / "qflash_b200.h"]
+SOURCES = [CSRC / "qflash_fwd.cu", CSRC / "qflash_quant.cu"]
+HEADERS = [CSRC / "sm100_ptx.cuh", CSRC / "qfb_internal.h", PKG.parent / "include" / "qflash_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared", "-Xptxas", "-v"]
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v"]
 
 
 def nvcc() -> str:
@@ -30,24 +31,43 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found; set NVCC or put the CUDA toolkit on PATH")
 
 
+OBJDIR = PKG / "_build"
+
+
+def _obj(src: Path) -> Path:
+    return OBJDIR / (src.stem + ".o")
+
+
+def _newer(a: Path, deps) -> bool:
+    return not a.exists() or any(p.exists() and p.stat().st_mtime > a.stat().st_mtime for p in deps)
+
+
 def stale() -> bool:
-    if not LIB.exists():
-        return True
-    t = LIB.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in SOURCES + HEADERS if p.exists())
+    return any(_newer(_obj(s), [s, *HEADERS]) for s in SOURCES) or _newer(LIB, [_obj(s) for s in SOURCES])
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not stale():
-        return LIB
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, *FLAGS, "-o", str(tmp), *map(str, SOURCES)]
+def _run(cmd, verbose):
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed ({r.returncode}):\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
     if verbose:
         sys.stderr.write(r.stderr)
-    os.replace(tmp, LIB)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile each source to an object (when it or a header changed), then
+    link the shared library."""
+    OBJDIR.mkdir(exist_ok=True)
+    objs = []
+    for src in SOURCES:
+        obj = _obj(src)
+        if force or _newer(obj, [src, *HEADERS]):
+            _run([nvcc(), *ARCH, *FLAGS, "-c", "-o", str(obj), str(src)], verbose)
+        objs.append(obj)
+    if force or _newer(LIB, objs):
+        tmp = LIB.with_suffix(".so.tmp")
+        _run([nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp), *map(str, objs)], verbose)
+        os.replace(tmp, LIB)
     return LIB
 
 

@@ -1,0 +1,19 @@
+// Declarations shared by the library's translation units (not part of the C ABI).
+#pragma once
+#include <cstdint>
+
+namespace qfb {
+
+int set_err(int code, const char* fmt, ...);
+int select_device(const void* p, int* dev);
+int sm_count(int dev);
+
+// The attention launch behind qflash_i8_fwd_ex; with `dparams` the fixed-point
+// constants are read from device memory (see KArgs::dparams).
+int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                  const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                  const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N,
+                  int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
+                  int32_t acc_shift, uint32_t flags, const long long* dparams, void* stream);
+
+}  // namespace qfb

@@ -62,6 +62,10 @@ struct KArgs {
   unsigned flags;
   int fast_exp;              // 1: 6-op exp2 form exact for every chunk; 2: exact while the row max < m_lim
   int m_lim;
+  // When set, the fixed-point constants come from device memory (written by
+  // the on-device parameter kernel): [0] status (non-zero: do nothing),
+  // [1] sm_rscale [2] exp_M [3] req_M [4] l_M [5] acc_M [6] m_lim.
+  const long long* dparams;
 };
 
 // ------------------------------------------------------------------ integer primitives
@@ -183,8 +187,19 @@ template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
 __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
     qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
-                   const KArgs a) {
+                   const KArgs a_in) {
   using C = Cfg<DQK, DV, BIAS, SEGS>;
+  KArgs a = a_in;
+  if (a_in.dparams) {
+    const long long* dp = a_in.dparams;
+    if (dp[0] != 0) return;  // the constants could not be formed (reported by the parameter kernel)
+    a.rs = (int)dp[1];
+    a.eM = (int)dp[2];
+    a.rM = (int)dp[3];
+    a.lM = dp[4];
+    a.accM = dp[5];
+    a.m_lim = (int)dp[6];
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
@@ -602,7 +617,7 @@ static thread_local std::string t_err;
 static std::atomic<uint64_t> g_launches{0};
 static std::atomic<int> g_last_grid{0};
 
-static int set_err(int code, const char* fmt, ...) {
+int set_err(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
   va_start(ap, fmt);
@@ -651,7 +666,7 @@ static int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, ui
 
 constexpr int kMaxDevices = 64;
 
-static int sm_count(int dev) {
+int sm_count(int dev) {
   static int n[kMaxDevices] = {0};
   if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
   return n[dev];
@@ -699,7 +714,7 @@ static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const C
 
 // Make the device that owns `p` current for this library's runtime (its
 // current-device state is separate from the caller's).
-static int select_device(const void* p, int* dev) {
+int select_device(const void* p, int* dev) {
   cudaPointerAttributes pa;
   if (cudaPointerGetAttributes(&pa, p) != cudaSuccess) {
     cudaGetLastError();
@@ -730,11 +745,13 @@ static int select_device(const void* p, int* dev) {
 
 using namespace qfb;
 
-extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
-                                const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
-                                const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z,
-                                int H, int N, int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M,
-                                int64_t acc_M, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream_) {
+namespace qfb {
+
+int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                  const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                  const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N,
+                  int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
+                  int32_t acc_shift, uint32_t flags, const long long* dparams, void* stream_) {
   cudaStream_t stream = (cudaStream_t)stream_;
   if (Z < 0 || H < 0 || N < 0) return set_err(QFLASH_ERR_ARG, "negative shape");
   if (!(D == 32 || D == 64 || D == 128 || D == 256)) return set_err(QFLASH_ERR_ARG, "head dim %d not in {32,64,128,256}", D);
@@ -743,7 +760,7 @@ extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* 
     return set_err(QFLASH_ERR_ARG, "null pointer");
   if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || o_strides[3] != 1)
     return set_err(QFLASH_ERR_ARG, "innermost (head-dim) stride must be 1");
-  if (sm_rscale <= 0) return set_err(QFLASH_ERR_ARG, "sm_rscale must be positive");
+  if (!dparams && sm_rscale <= 0) return set_err(QFLASH_ERR_ARG, "sm_rscale must be positive");
   if (l_shift < 1 || l_shift > 62 || acc_shift < 1 || acc_shift > 62) return set_err(QFLASH_ERR_ARG, "shift out of [1, 62]");
   if (bias && !bias_strides) return set_err(QFLASH_ERR_ARG, "bias without strides");
   int dev = 0;
@@ -786,7 +803,11 @@ extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* 
   // [-(S0 + m_new), 0].  x*exp_M + 2^16 fits int32 for |x| <= X1 and
   // r2 = x + (q+2)*rs fits for |x| <= X2, so rows with m_new <= min(X1, X2) - S0
   // are safe; if that holds for the largest possible m_new (D*2^14) it always holds.
-  {
+  if (dparams) {
+    // constants are produced on the device: the range check runs per chunk (m_lim from the device)
+    ka.dparams = dparams;
+    ka.fast_exp = bias ? 0 : 2;
+  } else {
     const long long S0 = ((long long)D << 14) > (1ll << 20) ? ((long long)D << 14) : (1ll << 20);
     const long long aem = -(long long)exp_M;
     const long long lim31 = (1ll << 31) - 1;
@@ -862,6 +883,18 @@ extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* 
     if (rc) return rc;
   }
   return QFLASH_OK;
+}
+
+}  // namespace qfb
+
+extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                                const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                                const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z,
+                                int H, int N, int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M,
+                                int64_t acc_M, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream) {
+  return qfb::attention_fwd(q, k, v, o, bias, q_strides, k_strides, v_strides, o_strides, bias_strides,
+                            bias_z_period, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags,
+                            nullptr, stream);
 }
 
 extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,

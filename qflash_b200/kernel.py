@@ -16,7 +16,10 @@ there and change no arithmetic, and this kernel has a single configuration.
 QFLASH_DIV selects the rounding of the final fp32 division acc / l:
 "ieee" (default; the reference's integer path as specified and as its
 interpreted run computes it) or "full" (the approximate fp32 divide that the
-reference's compiled GPU kernel uses).
+reference's compiled GPU kernel uses).  QFLASH_FUSED=1 routes qflash.forward
+(output mode) through ``forward_fused``: the same result without the host
+synchronisation; inputs for which the reference raises (all-zero q or k)
+then give an all-NaN output instead of an exception.
 """
 from __future__ import annotations
 
@@ -35,6 +38,7 @@ ACC_USE_SHIFT = os.environ.get("QFLASH_ACC_USE_SHIFT", "1") == "1"
 L_SHIFT = int(os.environ.get("QFLASH_L_SHIFT", "30"))
 ACC_SHIFT = int(os.environ.get("QFLASH_ACC_SHIFT", "30"))
 DIV_MODE = os.environ.get("QFLASH_DIV", "ieee")
+FUSED = os.environ.get("QFLASH_FUSED", "0") == "1"
 
 LOG2E = 1.44269504
 NEG_INF = -(1 << 20)
@@ -172,7 +176,63 @@ def qflash_forward(
 ):
     """Integer-only attention; same signature, arithmetic and output dtype as
     the reference's ``qflash.forward`` (qflash/kernel.py:275-351)."""
+    if FUSED and return_mode == 'output':
+        return forward_fused(query, key, value, attn_mask, scale)
     return forward_with_scales(query, key, value, attn_mask, scale, return_mode)
+
+
+def forward_fused(query, key, value, attn_mask=None, scale=None, bias_z_period=0, check=False,
+                  return_int8=False, return_workspace=False):
+    """``qflash.forward`` with every step on the device (``qflash_fwd_fused``):
+    no ``.item()`` synchronisation, no torch quantisation passes.  The output
+    equals ``qflash.forward``'s bit for bit (contiguous [Z, H, N, D], input
+    dtype).  ``check`` synchronises and raises where the reference raises
+    (ZeroDivisionError for an all-zero q or k); without it such inputs give
+    an all-NaN output.  ``bias_z_period`` as in ``forward_with_scales``."""
+    D = query.shape[-1]
+    assert query.shape[-1] == key.shape[-1] == value.shape[-1]
+    assert D in {16, 32, 64, 128, 256}
+    if D == 16:
+        raise ValueError("head dim 16 is not supported (the chunk width 32 exceeds it), as in the reference")
+    if not (query.is_cuda and key.is_cuda and value.is_cuda):
+        raise ValueError("qflash.forward runs on CUDA tensors only")
+    if query.dtype not in (torch.float32, torch.float16, torch.bfloat16) or not (
+            query.dtype == key.dtype == value.dtype):
+        raise ValueError(f"fused path takes float32/float16/bfloat16 inputs of one dtype, got {query.dtype}")
+    q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (query, key, value))
+    Z, H, N, _ = q.shape
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    mask, mstr, zb, hb = None, None, 0, 0
+    if attn_mask is not None:
+        m = attn_mask
+        while m.dim() < 4:
+            m = m.unsqueeze(0)
+        zb, hb = m.shape[0], m.shape[1]
+        if zb not in (1, Z, bias_z_period) or hb not in (1, H):
+            raise ValueError(f"attn_mask of shape {tuple(attn_mask.shape)} does not broadcast to {(Z, H, N, N)}")
+        m = m.expand(zb, hb, N, N)
+        mask = m
+        mstr = [0 if m.shape[i] == 1 else m.stride(i) for i in range(4)]
+    dev = q.device
+    q8, k8, v8, o8 = (torch.empty((Z, H, N, D), dtype=torch.int8, device=dev) for _ in range(4))
+    out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
+    ws = torch.empty(_lib.fused_workspace_bytes(zb, hb, N), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.fwd_fused(q, k, v, mask, mstr, zb, hb, bias_z_period if mask is not None else 0, q8, k8, v8, o8, out,
+                   scale * LOG2E, L_SHIFT, ACC_SHIFT, arith_flags(), ws, stream)
+    if check:
+        st = _lib.fused_status(ws, stream)
+        if st == 1:
+            raise ZeroDivisionError("float division by zero (q or k is all zero)")
+        if st != 0:
+            raise ValueError("the fixed-point constants are not representable for this input")
+    extra = []
+    if return_int8:
+        extra.append((q8, k8, v8, o8))
+    if return_workspace:
+        extra.append(ws)
+    return (out, *extra) if extra else out
 
 
 def tensor_scales(query: Tensor, key: Tensor, value: Tensor):
