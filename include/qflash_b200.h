@@ -111,6 +111,31 @@ size_t qflash_fused_workspace_bytes(int mask_zb, int mask_hb, int N);
  * 2 constants not representable (NaN/inf scales, or beyond int32). */
 int qflash_fused_status(const void* workspace, void* stream, int64_t* status);
 
+/*
+ * qflash_fwd_fused for callers that cannot allocate device memory -- their
+ * memory is owned by a pool or runtime they cannot extend, or cudaMalloc /
+ * cudaFree (which may synchronise the whole device) are not allowed on their
+ * path -- and so cannot pass a workspace.  No counterpart in the reference.
+ * Same arguments and result as qflash_fwd_fused without workspace /
+ * workspace_bytes; allocates nothing.  Its scratch is a fixed 4 MiB array in
+ * the library (every GPU that loads the library holds it until exit), enough
+ * for the constants plus an int32 bias of a mask up to about 4 MiB at
+ * [mask_zb, mask_hb, N, N rounded up to 4] int32; larger masks are rejected
+ * with QFLASH_ERR_UNSUPPORTED.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  Every call shares the one array: calls whose
+ * work overlaps on the GPU (other streams, other threads) race and corrupt
+ * each other; serialise them.  Nothing in the array needs to start at zero --
+ * each call writes every byte it later reads -- so stale contents from an
+ * earlier call are harmless.
+ */
+int qflash_fwd_fused_noalloc(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
+                             const int64_t k_strides[4], const int64_t v_strides[4], const void* mask,
+                             int mask_dtype, const int64_t mask_strides[4], int mask_zb, int mask_hb,
+                             int mask_z_period, int8_t* q8, int8_t* k8, int8_t* v8, int8_t* o8, void* out, int Z,
+                             int H, int N, int D, double scale_log2e, int32_t l_shift, int32_t acc_shift,
+                             uint32_t flags, void* stream);
+
 /* Reads and clears the device-side error word the kernels set when a bounded
  * wait gives up (0 = none).  Synchronises the stream. */
 int qflash_device_error(void* stream, uint32_t* out);

@@ -1,5 +1,6 @@
 // Declarations shared by the library's translation units (not part of the C ABI).
 #pragma once
+#include <cstddef>
 #include <cstdint>
 
 namespace qfb {
@@ -15,5 +16,14 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
                   const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N,
                   int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
                   int32_t acc_shift, uint32_t flags, const long long* dparams, void* stream);
+
+
+// The on-device forward behind qflash_fwd_fused and the workspace it needs.
+size_t fused_workspace_bytes(int bias_zb, int bias_hb, int N);
+int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
+              const int64_t k_strides[4], const int64_t v_strides[4], const void* mask, int mask_dtype,
+              const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period, int8_t* q8, int8_t* k8,
+              int8_t* v8, int8_t* o8, void* out, int Z, int H, int N, int D, double scale_log2e, int32_t l_shift,
+              int32_t acc_shift, uint32_t flags, void* ws, size_t ws_bytes, void* stream);
 
 }  // namespace qfb
