@@ -400,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       const int row = row0 + lane;
       const bool row_ok = row < a.N;
       int m = kNegInf, l = 1, alpha_prev = 0;
+      float pvb_prev = 0.f;
       // upper bound on max |acc| of this row, kept in fp32 with round-up margins
       float abound = 0.f;
       uint32_t acc[DV];  // acc + 2^31 (biased)
@@ -407,7 +408,8 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       for (int d = 0; d < DV; ++d) acc[d] = 0x80000000u;
 
       // acc = rescale(acc, alpha) + PV_gg; `first`: acc is still all zero
-      auto consume_pv = [&](uint32_t gg, int alpha, bool first) -> bool {
+      // pvb: upper bound on |PV_gg| of this row (128 * sum|P| of the chunk)
+      auto consume_pv = [&](uint32_t gg, int alpha, bool first, float pvb) -> bool {
         const int slot = gg & 1;
         if (!wait(pv_full(slot), (gg >> 1) & 1, kErrPvFull)) return false;
         tc_fence_after();
@@ -442,15 +444,22 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
               }
             }
           } else {
-#pragma unroll
+            // the general forms (64-bit product, idiv) are rare: a compact loop
+            // that takes acc[0] and rotates the array, so the hot loop stays small
+#pragma unroll 1
             for (int part = 0; part < DV / 32; ++part) {
               int pv[32];
               tmem_ld32(base + part * 32, pv);
-#pragma unroll
+#pragma unroll 1
               for (int d = 0; d < 32; ++d) {
-                const int x = (int)(acc[part * 32 + d] ^ 0x80000000u);
+                const int x = (int)(acc[0] ^ 0x80000000u);
                 const int r = acc_idiv ? rel_idiv(x, alpha, rs) : rel_shift64(x, (unsigned long long)A, S);
-                acc[part * 32 + d] = ((uint32_t)r + (uint32_t)pv[d]) ^ 0x80000000u;
+                const uint32_t nv = ((uint32_t)r + (uint32_t)pv[0]) ^ 0x80000000u;
+#pragma unroll
+                for (int i = 0; i < DV - 1; ++i) acc[i] = acc[i + 1];
+                acc[DV - 1] = nv;
+#pragma unroll
+                for (int i = 0; i < 31; ++i) pv[i] = pv[i + 1];
               }
             }
           }
@@ -462,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
                          ? __int_as_float(0x7f800000)
                          : __fmaf_ru(abound, aAbs * two_mS * 1.0001f, 2.f);
           }
-          abound = __fadd_ru(abound, 524288.f);  // + 2^19
+          abound = __fadd_ru(abound, pvb);
         }
         tc_fence_before();
         __syncwarp();
@@ -475,6 +484,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
         if (!(ok = wait(s_full(slot), (g >> 1) & 1, kErrSFull))) break;
         tc_fence_after();
         int alpha = 0;
+        float pvb = 0.f;
         if (active) {
           int s[32];
           tmem_ld32(tmem + lane_base + slot * C::S_COLS + sg * 32, s);
@@ -507,25 +517,64 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
           uint32_t pw[8];
           bool use_fast = MODE == kFast;
           if (MODE == kChecked) use_fast = __all_sync(0xffffffffu, m_new < a.m_lim);
+          // In a ragged last chunk every padded column holds NEG_INF, so all of
+          // them share one P value: groups of four columns past the last valid
+          // one (whole eighths of the chunk) take it without recomputation.
+          const int nq = nvalid >= kBN ? 4 : (nvalid + 7) >> 3;  // eighths-pairs with a valid column
           if (use_fast) {
             const int cm1 = (int)((0u - (unsigned)m_new) * (unsigned)eM + 65536u);
             const int c3 = (int)((unsigned)rs - (unsigned)m_new);
 #pragma unroll
+            for (int qd = 0; qd < 4; ++qd) {
+              if (qd > 0 && qd >= nq) {
+                const int ep = exp2_fast(kNegInf, eM, cm1, rs, c3);
+                const uint32_t pp = requant_pack4(ep, ep, ep, ep, rM);
+#pragma unroll
+                for (int c = 2 * qd; c < 8; ++c) pw[c] = pp;
+                break;
+              }
+#pragma unroll
+              for (int c = 2 * qd; c < 2 * qd + 2; ++c) {
+                const int e0 = exp2_fast(s[4 * c + 0], eM, cm1, rs, c3);
+                const int e1 = exp2_fast(s[4 * c + 1], eM, cm1, rs, c3);
+                const int e2 = exp2_fast(s[4 * c + 2], eM, cm1, rs, c3);
+                const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
+                pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+              }
+            }
+          } else if (MODE == kChecked) {
+            // rare fallback of the range-checked kernel: compact, rotating s and pw
+#pragma unroll 1
             for (int c = 0; c < 8; ++c) {
-              const int e0 = exp2_fast(s[4 * c + 0], eM, cm1, rs, c3);
-              const int e1 = exp2_fast(s[4 * c + 1], eM, cm1, rs, c3);
-              const int e2 = exp2_fast(s[4 * c + 2], eM, cm1, rs, c3);
-              const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
-              pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+              const int e0 = exp2_generic((int)((unsigned)s[0] - (unsigned)m_new), rs, eM, false);
+              const int e1 = exp2_generic((int)((unsigned)s[1] - (unsigned)m_new), rs, eM, false);
+              const int e2 = exp2_generic((int)((unsigned)s[2] - (unsigned)m_new), rs, eM, false);
+              const int e3 = exp2_generic((int)((unsigned)s[3] - (unsigned)m_new), rs, eM, false);
+              const uint32_t w = requant_pack4(e0, e1, e2, e3, rM);
+#pragma unroll
+              for (int i = 0; i < 28; ++i) s[i] = s[i + 4];
+#pragma unroll
+              for (int i = 0; i < 7; ++i) pw[i] = pw[i + 1];
+              pw[7] = w;
             }
           } else if (MODE != kFast) {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              const int e0 = exp2_generic((int)((unsigned)s[4 * c + 0] - (unsigned)m_new), rs, eM, exp_idiv);
-              const int e1 = exp2_generic((int)((unsigned)s[4 * c + 1] - (unsigned)m_new), rs, eM, exp_idiv);
-              const int e2 = exp2_generic((int)((unsigned)s[4 * c + 2] - (unsigned)m_new), rs, eM, exp_idiv);
-              const int e3 = exp2_generic((int)((unsigned)s[4 * c + 3] - (unsigned)m_new), rs, eM, exp_idiv);
-              pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+            for (int qd = 0; qd < 4; ++qd) {
+              if (qd > 0 && qd >= nq) {
+                const int ep = exp2_generic((int)((unsigned)kNegInf - (unsigned)m_new), rs, eM, exp_idiv);
+                const uint32_t pp = requant_pack4(ep, ep, ep, ep, rM);
+#pragma unroll
+                for (int c = 2 * qd; c < 8; ++c) pw[c] = pp;
+                break;
+              }
+#pragma unroll
+              for (int c = 2 * qd; c < 2 * qd + 2; ++c) {
+                const int e0 = exp2_generic((int)((unsigned)s[4 * c + 0] - (unsigned)m_new), rs, eM, exp_idiv);
+                const int e1 = exp2_generic((int)((unsigned)s[4 * c + 1] - (unsigned)m_new), rs, eM, exp_idiv);
+                const int e2 = exp2_generic((int)((unsigned)s[4 * c + 2] - (unsigned)m_new), rs, eM, exp_idiv);
+                const int e3 = exp2_generic((int)((unsigned)s[4 * c + 3] - (unsigned)m_new), rs, eM, exp_idiv);
+                pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+              }
             }
           }
           alpha = exp2_generic((int)((unsigned)m - (unsigned)m_new), rs, eM, exp_idiv);
@@ -541,27 +590,33 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
                                 : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
           l = (int)((unsigned)lr + (unsigned)ls0 + (unsigned)ls1);
           m = m_new;
+          // |PV| <= 128 * sum|P|; sum|P| = ls0 + ls1 unless some P byte is negative
+          const uint32_t neg = ((pw[0] | pw[1] | pw[2] | pw[3]) | (pw[4] | pw[5] | pw[6] | pw[7])) & 0x80808080u;
+          pvb = neg ? 524288.f : (float)((ls0 + ls1) << 7);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(slot));
-        if (j > 0 && !(ok = consume_pv(g - 1, alpha_prev, j == 1))) break;
+        if (j > 0 && !(ok = consume_pv(g - 1, alpha_prev, j == 1, pvb_prev))) break;
         alpha_prev = alpha;
+        pvb_prev = pvb;
       }
       if (!ok) break;
-      if (!(ok = consume_pv(g - 1, alpha_prev, nch == 1))) break;
+      if (!(ok = consume_pv(g - 1, alpha_prev, nch == 1, pvb_prev))) break;
 
       // epilogue: O row = int8(int32(fp32(acc) / fp32(l)))
       if (active) {
         int8_t* orow = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row * a.os_n + a.v_col0;
         // Exact shortcut: for |acc| < 2^23 and 0 < l < 2^24, trunc(RN_f32(acc / l))
         // equals the truncated integer quotient (rounding up to an integer n >= 2
-        // needs l >= 2^24 / n, i.e. |acc| >= 2^23).  The quotient is a rounded
-        // float estimate (off by at most one) fixed by an exact remainder check.
+        // needs l >= 2^24 / n, i.e. |acc| >= 2^23).  That quotient is
+        // floor(|acc| * RU(1/l)) taken with one round-toward-zero FMA:
+        // RU(1/l) - 1/l < 2^-23 / l, so |acc| * RU(1/l) lies in
+        // [|acc| / l, |acc| / l + 1/l), below the next integer.
         const bool fast_div = !div_full && l > 0 && l < (1 << 24) && abound < 8388607.f;
         uint32_t res[DV / 4];
         if (__all_sync(0xffffffffu, fast_div || !row_ok)) {
-          const float rcp = __frcp_rn((float)l);
+          const float rcp = __frcp_ru((float)l);
 #pragma unroll
           for (int w4 = 0; w4 < DV / 4; ++w4) {
             int r4[4];
@@ -570,19 +625,23 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
               const int x = (int)(acc[w4 * 4 + b] ^ 0x80000000u);
               const int ux = abs(x);
               const float af = __int_as_float(ux | 0x4B000000) - 8388608.0f;
-              int qd = __float_as_int(__fmaf_rn(af, rcp, 8388608.0f)) - 0x4B000000;
-              qd += (ux - qd * l) >> 31;
+              const int qd = __float_as_int(__fmaf_rz(af, rcp, 8388608.0f)) - 0x4B000000;
               r4[b] = x < 0 ? -qd : qd;
             }
             res[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
           }
         } else {
-#pragma unroll
+          // rare: the literal fp32 division, compact (acc[0..3] per step, rotating)
+#pragma unroll 1
           for (int w4 = 0; w4 < DV / 4; ++w4) {
             int r4[4];
 #pragma unroll
-            for (int b = 0; b < 4; ++b) r4[b] = div_to_i32((int)(acc[w4 * 4 + b] ^ 0x80000000u), l, div_full);
-            res[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
+            for (int b = 0; b < 4; ++b) r4[b] = div_to_i32((int)(acc[b] ^ 0x80000000u), l, div_full);
+#pragma unroll
+            for (int i = 0; i < DV - 4; ++i) acc[i] = acc[i + 4];
+#pragma unroll
+            for (int i = 0; i < DV / 4 - 1; ++i) res[i] = res[i + 1];
+            res[DV / 4 - 1] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
           }
         }
         if (row_ok) {
