@@ -161,14 +161,18 @@ struct Cfg {
   static constexpr int OFF_V = OFF_K + KVS * K_BYTES;
   static constexpr int OFF_B = OFF_V + KVS * V_BYTES;
   static constexpr int OFF_BAR = OFF_B + KVS * B_BYTES;
-  static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2 + 2;
+  static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr int S_COLS = 32 * SEGS;           // one S slot: a 32-column region per segment
-  static constexpr int PV_OFF = 2 * S_COLS;          // TMEM column of PV slot 0
-  static constexpr int PV_SLOT = SEGS * DV;
-  static constexpr int TMEM_NEED = PV_OFF + 2 * PV_SLOT;
+  static constexpr int ACC_OFF = 2 * S_COLS;         // TMEM column of acc (DV columns per segment)
+  static constexpr int TMEM_NEED = ACC_OFF + SEGS * DV;
   static constexpr int TMEM_COLS = TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512);
+  // resident CTAs the register budget is compiled for: what TMEM allows, at most
+  // 2 (a third CTA per SM measured slower: the SM's shared units saturate first)
+  static constexpr int MIN_CTAS = (512 / TMEM_COLS) < 2 ? (512 / TMEM_COLS) : 2;
+  // registers per thread for MIN_CTAS CTAs of kThreads threads (multiple of 8)
+  static constexpr int MAX_REGS = (65536 / (MIN_CTAS * kThreads)) / 8 * 8 > 255 ? 255 : (65536 / (MIN_CTAS * kThreads)) / 8 * 8;
   static constexpr uint32_t IDESC_S = idesc_i8(kBM, kBN, false);
   static constexpr uint32_t IDESC_PV = idesc_i8(kBM, DV, true);
   static constexpr uint32_t SWQ = QA == 32 ? kSw32 : (QA == 64 ? kSw64 : kSw128);
@@ -184,7 +188,7 @@ struct Cfg {
 enum Mode : int { kGen = 0, kFast = 1, kChecked = 2, kPlain = 3 };
 
 template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
-__global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
+__global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS>::MAX_REGS))
     qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
                    const KArgs a_in) {
@@ -213,8 +217,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
   auto kv_empty = [&](int i) { return bar0 + 8u * (4 + C::KVS + i); };
   auto s_full = [&](int i) { return bar0 + 8u * (4 + 2 * C::KVS + i); };
   auto p_full = [&](int i) { return bar0 + 8u * (6 + 2 * C::KVS + i); };
-  auto pv_full = [&](int i) { return bar0 + 8u * (8 + 2 * C::KVS + i); };
-  auto pv_empty = [&](int i) { return bar0 + 8u * (10 + 2 * C::KVS + i); };
+  auto acc_full = [&](int i) { return bar0 + 8u * (8 + 2 * C::KVS + i); };
   uint32_t* tmem_slot = (uint32_t*)(smem + C::OFF_MISC);
   volatile int* abort_flag = (volatile int*)(smem + C::OFF_MISC + 4);
 
@@ -224,8 +227,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       mbar_init(q_empty(i), 1);
       mbar_init(s_full(i), 1);
       mbar_init(p_full(i), 4);
-      mbar_init(pv_full(i), 1);
-      mbar_init(pv_empty(i), 4);
+      mbar_init(acc_full(i), 1);
     }
     for (int i = 0; i < C::KVS; ++i) {
       mbar_init(kv_full(i), 1);
@@ -261,6 +263,16 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
   };
 
   const int nch = a.nch;
+  // Work item of round k for this CTA.  Rounds alternate direction over the
+  // CTAs (k*G + b, then k*G + G-1-b), so a CTA alternates between the tiles of
+  // a head (the last tile of a head is often partial) while every round still
+  // covers one contiguous range of items (the tiles of a head run together and
+  // share K/V in L2).  A negative value ends the loop.
+  auto item_of = [&](int k) -> int {
+    const long long G = gridDim.x, b = blockIdx.x;
+    const long long it = (long long)k * G + ((k & 1) ? G - 1 - b : b);
+    return it < a.nitems ? (int)it : -1;
+  };
   // head (z, h) and first query row of segment `sg` of work item `item`; false if the segment is empty
   auto decode = [&](int item, int sg, int& z, int& h, int& row0) -> bool {
     int zh;
@@ -286,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       uint32_t kv_it = 0;
       int qi = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x, ++qi) {
+      for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k), ++qi) {
         int nseg = 0;
         for (int sg = 0; sg < SEGS; ++sg) {
           int z, h, r0;
@@ -329,23 +341,24 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       uint32_t g = 0;
       int qi = 0;
       bool ok = true;
-      auto issue_pv = [&](uint32_t gg) -> bool {
+      // acc (+)= P_gg V_gg straight into the TMEM accumulator, once the softmax
+      // warps have written P_gg and rescaled acc; `init` starts a new item
+      auto issue_pv = [&](uint32_t gg, bool init) -> bool {
         const int slot = gg & 1;
         const int st = gg % C::KVS;
         if (!wait(p_full(slot), (gg >> 1) & 1, kErrPFull)) return false;
-        if (!wait(pv_empty(slot), ((gg >> 1) & 1) ^ 1, kErrPvEmpty)) return false;
         tc_fence_after();
 #pragma unroll
         for (int sg = 0; sg < SEGS; ++sg) {
           const uint64_t bdesc =
               smem_desc(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, kBN * C::VA, 8 * C::VA, C::SWV);
-          mma_i8_ts(tmem + C::PV_OFF + slot * C::PV_SLOT + sg * DV, tmem + slot * C::S_COLS, bdesc, C::IDESC_PV, 0);
+          mma_i8_ts(tmem + C::ACC_OFF + sg * DV, tmem + slot * C::S_COLS, bdesc, C::IDESC_PV, init ? 0u : 1u);
         }
-        tc_commit(pv_full(slot));
+        tc_commit(acc_full(slot));
         tc_commit(kv_empty(st));
         return true;
       };
-      for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x, ++qi) {
+      for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k), ++qi) {
         const int qb = qi & 1;
         if (!(ok = wait(q_full(qb), (qi >> 1) & 1, kErrQFull))) break;
         tc_fence_after();
@@ -368,9 +381,9 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
           }
           tc_commit(s_full(g & 1));
           if (j == nch - 1) tc_commit(q_empty(qb));
-          if (j > 0 && !(ok = issue_pv(g - 1))) break;
+          if (j > 0 && !(ok = issue_pv(g - 1, j == 1))) break;
         }
-        if (ok) ok = issue_pv(g - 1);
+        if (ok) ok = issue_pv(g - 1, nch == 1);
       }
     }
   } else {
@@ -390,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
     const float two_mS = __int_as_float((127 - S) << 23);  // 2^-S
     uint32_t g = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < a.nitems; item += gridDim.x) {
+    for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k)) {
       // warp -> segment (head) and its 32-row slice
       const int sg = SEGS == 1 ? 0 : warp / (4 / SEGS);
       int z, h, rbase;
@@ -399,83 +412,51 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
       const bool active = seg_ok && row0 < a.N;
       const int row = row0 + lane;
       const bool row_ok = row < a.N;
-      int m = kNegInf, l = 1, alpha_prev = 0;
-      float pvb_prev = 0.f;
+      int m = kNegInf, l = 1;
       // upper bound on max |acc| of this row, kept in fp32 with round-up margins
       float abound = 0.f;
-      uint32_t acc[DV];  // acc + 2^31 (biased)
-#pragma unroll
-      for (int d = 0; d < DV; ++d) acc[d] = 0x80000000u;
+      // acc lives in TMEM (this warp's lanes, DV columns); PV MMAs accumulate into it
+      const uint32_t acc_base = tmem + lane_base + C::ACC_OFF + sg * DV;
 
-      // acc = rescale(acc, alpha) + PV_gg; `first`: acc is still all zero
-      // pvb: upper bound on |PV_gg| of this row (128 * sum|P| of the chunk)
-      auto consume_pv = [&](uint32_t gg, int alpha, bool first, float pvb) -> bool {
-        const int slot = gg & 1;
-        if (!wait(pv_full(slot), (gg >> 1) & 1, kErrPvFull)) return false;
+      // acc = rel(acc, alpha) in place, once PV_gg (the previous chunk's) has landed
+      auto rescale = [&](uint32_t gg, int alpha, long long A) -> bool {
+        if (!wait(acc_full(gg & 1), (gg >> 1) & 1, kErrPvFull)) return false;
         tc_fence_after();
-        if (active) {
-          const long long A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
-          const bool ident = !acc_idiv && alpha == rs && abound < ident_lim;
-          const bool skip = first || __all_sync(0xffffffffu, ident || !row_ok);
-          const bool fast = !acc_idiv && S < 32 && A >= 0 && A < (1ll << 32);
-          const int mode = skip ? 0 : (__all_sync(0xffffffffu, fast) ? 1 : 2);
-          const uint32_t base = tmem + lane_base + C::PV_OFF + slot * C::PV_SLOT + sg * DV;
-          if (mode == 0) {
+        const bool fast = !acc_idiv && S < 32 && A >= 0 && A < (1ll << 31);
+        if (__all_sync(0xffffffffu, fast || !row_ok)) {
+          // int32((x * A + 2^(S-1)) >> S): one signed wide multiply-add and a funnel shift
+          const int A32 = (int)A;
+          const long long half = 1ll << (S - 1);
 #pragma unroll
-            for (int part = 0; part < DV / 32; ++part) {
-              int pv[32];
-              tmem_ld32(base + part * 32, pv);
+          for (int part = 0; part < DV / 32; ++part) {
+            int v[32];
+            tmem_ld32(acc_base + part * 32, v);
 #pragma unroll
-              for (int d = 0; d < 32; ++d) acc[part * 32 + d] += (uint32_t)pv[d];
+            for (int d = 0; d < 32; ++d) {
+              long long w;
+              asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(w) : "r"(v[d]), "r"(A32), "l"(half));
+              v[d] = (int)__funnelshift_r((uint32_t)w, (uint32_t)((unsigned long long)w >> 32), S);
             }
-          } else if (mode == 1) {
-            const unsigned long long Cst =
-                (1ull << (S - 1)) - ((unsigned long long)A << 31) + (1ull << ((S + 31) & 63));
-            const uint32_t A32 = (uint32_t)A;
-#pragma unroll
-            for (int part = 0; part < DV / 32; ++part) {
-              int pv[32];
-              tmem_ld32(base + part * 32, pv);
-#pragma unroll
-              for (int d = 0; d < 32; ++d) {
-                unsigned long long w;
-                asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(w) : "r"(acc[part * 32 + d]), "r"(A32), "l"(Cst));
-                acc[part * 32 + d] = __funnelshift_r((uint32_t)w, (uint32_t)(w >> 32), S) + (uint32_t)pv[d];
-              }
-            }
-          } else {
-            // the general forms (64-bit product, idiv) are rare: a compact loop
-            // that takes acc[0] and rotates the array, so the hot loop stays small
-#pragma unroll 1
-            for (int part = 0; part < DV / 32; ++part) {
-              int pv[32];
-              tmem_ld32(base + part * 32, pv);
-#pragma unroll 1
-              for (int d = 0; d < 32; ++d) {
-                const int x = (int)(acc[0] ^ 0x80000000u);
-                const int r = acc_idiv ? rel_idiv(x, alpha, rs) : rel_shift64(x, (unsigned long long)A, S);
-                const uint32_t nv = ((uint32_t)r + (uint32_t)pv[0]) ^ 0x80000000u;
-#pragma unroll
-                for (int i = 0; i < DV - 1; ++i) acc[i] = acc[i + 1];
-                acc[DV - 1] = nv;
-#pragma unroll
-                for (int i = 0; i < 31; ++i) pv[i] = pv[i + 1];
-              }
-            }
+            tmem_st32(acc_base + part * 32, v);
           }
-          // |rel(x)| <= |x| * |A| / 2^S + 1 (the idiv form: <= |x| * |alpha| / rs + 1)
-          // (no bound when a 64-bit product could wrap or in the idiv form)
-          if (!first) {
-            const float aAbs = fabsf((float)A);
-            abound = (acc_idiv || S > 31 || abound * aAbs >= 4.6e18f)
-                         ? __int_as_float(0x7f800000)
-                         : __fmaf_ru(abound, aAbs * two_mS * 1.0001f, 2.f);
+        } else {
+          // the general forms (64-bit product, idiv) are rare: a compact loop
+          // that takes v[0] and rotates the array
+#pragma unroll 1
+          for (int part = 0; part < DV / 32; ++part) {
+            int v[32];
+            tmem_ld32(acc_base + part * 32, v);
+#pragma unroll 1
+            for (int d = 0; d < 32; ++d) {
+              const int r = acc_idiv ? rel_idiv(v[0], alpha, rs) : rel_shift64(v[0], (unsigned long long)A, S);
+#pragma unroll
+              for (int i = 0; i < 31; ++i) v[i] = v[i + 1];
+              v[31] = r;
+            }
+            tmem_st32(acc_base + part * 32, v);
           }
-          abound = __fadd_ru(abound, pvb);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(pv_empty(slot));
+        tmem_wait_st();
         return true;
       };
 
@@ -484,7 +465,6 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
         if (!(ok = wait(s_full(slot), (g >> 1) & 1, kErrSFull))) break;
         tc_fence_after();
         int alpha = 0;
-        float pvb = 0.f;
         if (active) {
           int s[32];
           tmem_ld32(tmem + lane_base + slot * C::S_COLS + sg * 32, s);
@@ -590,22 +570,34 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
                                 : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
           l = (int)((unsigned)lr + (unsigned)ls0 + (unsigned)ls1);
           m = m_new;
+          // acc = rel(acc, alpha) before PV of this chunk is added (first chunk: acc
+          // starts from PV alone).  Skipped when it is the identity for every row
+          // of the warp: alpha == rs and |acc| * |rs * acc_M - 2^S| < 2^(S-1).
+          if (j > 0) {
+            const long long A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
+            const bool ident = !acc_idiv && alpha == rs && abound < ident_lim;
+            if (!__all_sync(0xffffffffu, ident || !row_ok) && !(ok = rescale(g - 1, alpha, A))) break;
+            // |rel(x)| <= |x| * |A| / 2^S + 1 (the idiv form: <= |x| * |alpha| / rs + 1)
+            // (no bound when a 64-bit product could wrap or in the idiv form)
+            const float aAbs = fabsf((float)A);
+            abound = (acc_idiv || S > 31 || abound * aAbs >= 4.6e18f)
+                         ? __int_as_float(0x7f800000)
+                         : __fmaf_ru(abound, aAbs * two_mS * 1.0001f, 2.f);
+          }
           // |PV| <= 128 * sum|P|; sum|P| = ls0 + ls1 unless some P byte is negative
           const uint32_t neg = ((pw[0] | pw[1] | pw[2] | pw[3]) | (pw[4] | pw[5] | pw[6] | pw[7])) & 0x80808080u;
-          pvb = neg ? 524288.f : (float)((ls0 + ls1) << 7);
+          abound = __fadd_ru(abound, neg ? 524288.f : (float)((ls0 + ls1) << 7));
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(slot));
-        if (j > 0 && !(ok = consume_pv(g - 1, alpha_prev, j == 1, pvb_prev))) break;
-        alpha_prev = alpha;
-        pvb_prev = pvb;
       }
       if (!ok) break;
-      if (!(ok = consume_pv(g - 1, alpha_prev, nch == 1, pvb_prev))) break;
 
-      // epilogue: O row = int8(int32(fp32(acc) / fp32(l)))
+      // epilogue: O row = int8(int32(fp32(acc) / fp32(l))), once the last PV has landed
       if (active) {
+        if (!(ok = wait(acc_full((g - 1) & 1), ((g - 1) >> 1) & 1, kErrPvFull))) break;
+        tc_fence_after();
         int8_t* orow = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row * a.os_n + a.v_col0;
         // Exact shortcut: for |acc| < 2^23 and 0 < l < 2^24, trunc(RN_f32(acc / l))
         // equals the truncated integer quotient (rounding up to an integer n >= 2
@@ -614,45 +606,49 @@ __global__ void __launch_bounds__(kThreads, (DV <= 64 ? 2 : 1))
         // RU(1/l) - 1/l < 2^-23 / l, so |acc| * RU(1/l) lies in
         // [|acc| / l, |acc| / l + 1/l), below the next integer.
         const bool fast_div = !div_full && l > 0 && l < (1 << 24) && abound < 8388607.f;
-        uint32_t res[DV / 4];
-        if (__all_sync(0xffffffffu, fast_div || !row_ok)) {
-          const float rcp = __frcp_ru((float)l);
+        const bool fastw = __all_sync(0xffffffffu, fast_div || !row_ok);
+        const float rcp = __frcp_ru((float)l);
 #pragma unroll
-          for (int w4 = 0; w4 < DV / 4; ++w4) {
-            int r4[4];
+        for (int part = 0; part < DV / 32; ++part) {
+          int v[32];
+          tmem_ld32(acc_base + part * 32, v);
+          uint32_t res[8];
+          if (fastw) {
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const int x = (int)(acc[w4 * 4 + b] ^ 0x80000000u);
-              const int ux = abs(x);
-              const float af = __int_as_float(ux | 0x4B000000) - 8388608.0f;
-              const int qd = __float_as_int(__fmaf_rz(af, rcp, 8388608.0f)) - 0x4B000000;
-              r4[b] = x < 0 ? -qd : qd;
+            for (int w4 = 0; w4 < 8; ++w4) {
+              int r4[4];
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                const int x = v[w4 * 4 + b];
+                const int ux = abs(x);
+                const float af = __int_as_float(ux | 0x4B000000) - 8388608.0f;
+                const int qd = __float_as_int(__fmaf_rz(af, rcp, 8388608.0f)) - 0x4B000000;
+                r4[b] = x < 0 ? -qd : qd;
+              }
+              res[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
             }
-            res[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
-          }
-        } else {
-          // rare: the literal fp32 division, compact (acc[0..3] per step, rotating)
-#pragma unroll 1
-          for (int w4 = 0; w4 < DV / 4; ++w4) {
-            int r4[4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) r4[b] = div_to_i32((int)(acc[b] ^ 0x80000000u), l, div_full);
-#pragma unroll
-            for (int i = 0; i < DV - 4; ++i) acc[i] = acc[i + 4];
-#pragma unroll
-            for (int i = 0; i < DV / 4 - 1; ++i) res[i] = res[i + 1];
-            res[DV / 4 - 1] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
-          }
-        }
-        if (row_ok) {
-          if (a.o_vec16) {
-#pragma unroll
-            for (int c = 0; c < DV / 16; ++c)
-              *(int4*)(orow + c * 16) = make_int4((int)res[4 * c], (int)res[4 * c + 1], (int)res[4 * c + 2],
-                                                  (int)res[4 * c + 3]);
           } else {
+            // rare: the literal fp32 division, compact (v[0..3] per step, rotating)
+#pragma unroll 1
+            for (int w4 = 0; w4 < 8; ++w4) {
+              int r4[4];
 #pragma unroll
-            for (int b = 0; b < DV; ++b) orow[b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
+              for (int b = 0; b < 4; ++b) r4[b] = div_to_i32(v[b], l, div_full);
+#pragma unroll
+              for (int i = 0; i < 28; ++i) v[i] = v[i + 4];
+#pragma unroll
+              for (int i = 0; i < 7; ++i) res[i] = res[i + 1];
+              res[7] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
+            }
+          }
+          if (row_ok) {
+            if (a.o_vec16) {
+              *(int4*)(orow + part * 32) = make_int4((int)res[0], (int)res[1], (int)res[2], (int)res[3]);
+              *(int4*)(orow + part * 32 + 16) = make_int4((int)res[4], (int)res[5], (int)res[6], (int)res[7]);
+            } else {
+#pragma unroll
+              for (int b = 0; b < 32; ++b) orow[part * 32 + b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
+            }
           }
         }
       }
