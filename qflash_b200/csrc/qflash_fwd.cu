@@ -41,6 +41,7 @@ constexpr int kBM = 128;             // query rows per tile = TMEM lanes
 constexpr int kBN = 32;              // keys per chunk (BLOCK_N of the reference)
 constexpr int kNegInf = -(1 << 20);  // qflash/kernel.py:137
 constexpr int kThreads = 192;
+constexpr uint32_t kWaitHintNs = 100000;  // longest sleep of one try_wait (0.1 ms)
 
 __device__ unsigned int g_err;       // set when a bounded wait gives up
 
@@ -120,6 +121,17 @@ __device__ __forceinline__ uint32_t requant_pack4(int e0, int e1, int e2, int e3
 __device__ __forceinline__ int rel_shift64(int x, unsigned long long A, int S) {
   const unsigned long long v = (unsigned long long)(long long)x * A + (1ull << (S - 1));
   return (int)((long long)v >> S);
+}
+// scale_release_shift on the FP64 pipe.  With Cd = 1.5*2^(51+S) + 2^(S-1):
+// (double)x is exact (2^52 + (x + 2^31), minus 2^52 + 2^31); x*A + Cd stays in
+// the binade [2^(51+S), 2^(52+S)) (|x*A| < 2^62, S >= 13), where one ulp is
+// 2^(S-1), so the FMA rounded down yields 1.5*2^52 + w in ulps with
+// w = floor((x*A + 2^(S-1)) / 2^(S-1)); bits [1, 33) of its encoding are
+// floor(w / 2) = rel(x) (mod 2^32).  Needs 0 <= A < 2^31.
+__device__ __forceinline__ int rel_fp64(int x, double Ad, double Cd) {
+  const double xd = __hiloint2double(0x43300000, x ^ (int)0x80000000) - 4503601774854144.0;  // 2^52 + 2^31
+  const double y = __fma_rd(xd, Ad, Cd);
+  return (int)__funnelshift_r((uint32_t)__double2loint(y), (uint32_t)__double2hiint(y), 1);
 }
 // scale_release_idiv (qflash/kernel.py:72-74): (x * alpha) // rs, int32 product.
 __device__ __forceinline__ int rel_idiv(int x, int alpha, int rs) {
@@ -249,10 +261,13 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     atomicOr(&g_err, code);
     *abort_flag = 1;
   };
+  // Bounded wait: each try_wait may sleep up to kWaitHintNs (waking when the
+  // phase completes), so a waiting warp takes few issue slots from the others;
+  // the abort flag and the ~2 s limit are checked once per sleep.
   auto wait = [&](uint32_t bar, uint32_t parity, unsigned code) -> bool {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_hint(bar, parity, kWaitHintNs)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_hint(bar, parity, kWaitHintNs)) {
       if (*abort_flag) return false;
       if (clock64() - t0 > kWaitCycles) {
         fail(code);
@@ -422,21 +437,17 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
       auto rescale = [&](uint32_t gg, int alpha, long long A) -> bool {
         if (!wait(acc_full(gg & 1), (gg >> 1) & 1, kErrPvFull)) return false;
         tc_fence_after();
-        const bool fast = !acc_idiv && S < 32 && A >= 0 && A < (1ll << 31);
+        const bool fast = !acc_idiv && S >= 13 && A >= 0 && A < (1ll << 31);
         if (__all_sync(0xffffffffu, fast || !row_ok)) {
-          // int32((x * A + 2^(S-1)) >> S): one signed wide multiply-add and a funnel shift
-          const int A32 = (int)A;
-          const long long half = 1ll << (S - 1);
+          // int32((x * A + 2^(S-1)) >> S) on the FP64 pipe (rel_fp64)
+          const double Ad = (double)A;
+          const double Cd = __longlong_as_double(((1023ll + 51 + S) << 52) | (1ll << 51) | 1ll);
 #pragma unroll
           for (int part = 0; part < DV / 32; ++part) {
             int v[32];
             tmem_ld32(acc_base + part * 32, v);
 #pragma unroll
-            for (int d = 0; d < 32; ++d) {
-              long long w;
-              asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(w) : "r"(v[d]), "r"(A32), "l"(half));
-              v[d] = (int)__funnelshift_r((uint32_t)w, (uint32_t)((unsigned long long)w >> 32), S);
-            }
+            for (int d = 0; d < 32; ++d) v[d] = rel_fp64(v[d], Ad, Cd);
             tmem_st32(acc_base + part * 32, v);
           }
         } else {
