@@ -416,6 +416,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     const long long delta0 = (long long)rs * a.accM - (1ll << S);
     const float ident_lim = (float)(1ull << (S - 1)) * 0.999f / (float)(delta0 < 0 ? -delta0 : (delta0 ? delta0 : 1));
     const float two_mS = __int_as_float((127 - S) << 23);  // 2^-S
+    const float accM_ru = __ll2float_ru(a.accM < 0 ? -a.accM : a.accM);
     uint32_t g = 0;
     bool ok = true;
     for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k)) {
@@ -475,7 +476,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
         const int slot = g & 1;
         if (!(ok = wait(s_full(slot), (g >> 1) & 1, kErrSFull))) break;
         tc_fence_after();
-        int alpha = 0;
+        int alpha = 0, m_new = m;
+        uint32_t pw[8];
         if (active) {
           int s[32];
           tmem_ld32(tmem + lane_base + slot * C::S_COLS + sg * 32, s);
@@ -504,8 +506,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
 #pragma unroll
           for (int c = 0; c < 4; ++c) t16[c] = max(t16[c], t16[c + 4]);
           const int mx = max(max(t16[0], t16[2]), max(t16[1], t16[3]));
-          const int m_new = max(m, mx);
-          uint32_t pw[8];
+          m_new = max(m, mx);
           bool use_fast = MODE == kFast;
           if (MODE == kChecked) use_fast = __all_sync(0xffffffffu, m_new < a.m_lim);
           // In a ragged last chunk every padded column holds NEG_INF, so all of
@@ -570,6 +571,21 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
           }
           alpha = exp2_generic((int)((unsigned)m - (unsigned)m_new), rs, eM, exp_idiv);
           tmem_st8(tmem + lane_base + slot * C::S_COLS, pw);
+          // acc = rel(acc, alpha) before PV of this chunk is added (first chunk: acc
+          // starts from PV alone).  Skipped when it is the identity for every row
+          // of the warp: alpha == rs and |acc| * |rs * acc_M - 2^S| < 2^(S-1).
+          if (j > 0) {
+            const long long A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
+            const bool ident = !acc_idiv && alpha == rs && abound < ident_lim;
+            if (!__all_sync(0xffffffffu, ident || !row_ok) && !(ok = rescale(g - 1, alpha, A))) break;
+          }
+        }
+        // P and acc are ready: release the MMA warp before the bookkeeping below,
+        // which only later chunks need
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(slot));
+        if (active) {
           // l_j = sum of the 32 int8 P values, two independent dot-product chains
           int ls0 = 0, ls1 = 0;
 #pragma unroll
@@ -581,16 +597,11 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
                                 : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
           l = (int)((unsigned)lr + (unsigned)ls0 + (unsigned)ls1);
           m = m_new;
-          // acc = rel(acc, alpha) before PV of this chunk is added (first chunk: acc
-          // starts from PV alone).  Skipped when it is the identity for every row
-          // of the warp: alpha == rs and |acc| * |rs * acc_M - 2^S| < 2^(S-1).
           if (j > 0) {
-            const long long A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
-            const bool ident = !acc_idiv && alpha == rs && abound < ident_lim;
-            if (!__all_sync(0xffffffffu, ident || !row_ok) && !(ok = rescale(g - 1, alpha, A))) break;
-            // |rel(x)| <= |x| * |A| / 2^S + 1 (the idiv form: <= |x| * |alpha| / rs + 1)
-            // (no bound when a 64-bit product could wrap or in the idiv form)
-            const float aAbs = fabsf((float)A);
+            // |rel(x)| <= |x| * |A| / 2^S + 1 (the idiv form: <= |x| * |alpha| / rs + 1),
+            // |A| = |alpha| * acc_M taken in float with round-up; no bound when the
+            // 64-bit product could wrap, or in the idiv form
+            const float aAbs = __fmul_ru(__uint2float_ru(alpha < 0 ? 0u - (unsigned)alpha : (unsigned)alpha), accM_ru);
             abound = (acc_idiv || S > 31 || abound * aAbs >= 4.6e18f)
                          ? __int_as_float(0x7f800000)
                          : __fmaf_ru(abound, aAbs * two_mS * 1.0001f, 2.f);
@@ -599,9 +610,6 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
           const uint32_t neg = ((pw[0] | pw[1] | pw[2] | pw[3]) | (pw[4] | pw[5] | pw[6] | pw[7])) & 0x80808080u;
           abound = __fadd_ru(abound, neg ? 524288.f : (float)((ls0 + ls1) << 7));
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(p_full(slot));
       }
       if (!ok) break;
 
