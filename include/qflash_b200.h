@@ -103,6 +103,21 @@ int qflash_fwd_fused(const void* q, const void* k, const void* v, int dtype, con
                      int32_t l_shift, int32_t acc_shift, uint32_t flags, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/*
+ * qflash_fwd_fused without the int8 output buffer: the attention epilogue
+ * writes int8(acc / l) * o_scale straight into `out` (the input dtype) at the
+ * element strides `out_strides` (NULL: contiguous [Z, H, N, D]; the head-dim
+ * stride must be 1), e.g. the [Z, N, H, D] layout QAttention reshapes to
+ * (qflash/attention.py:26) without a copy.  Replaces kernel.py:347-351 (the
+ * int8 O tensor and o * o_scale).  On a status other than 0 `out` is all NaN.
+ */
+int qflash_fwd_fused_out(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
+                         const int64_t k_strides[4], const int64_t v_strides[4], const void* mask, int mask_dtype,
+                         const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period, int8_t* q8,
+                         int8_t* k8, int8_t* v8, void* out, const int64_t out_strides[4], int Z, int H, int N, int D,
+                         double scale_log2e, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Workspace bytes qflash_fwd_fused needs (mask_zb = mask_hb = 0 without a mask). */
 size_t qflash_fused_workspace_bytes(int mask_zb, int mask_hb, int N);
 

@@ -41,6 +41,12 @@ SIGNATURES = {
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int32, ctypes.c_int32,
         ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "qflash_fwd_fused_out": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, _I64x4, _I64x4, _I64x4,
+        ctypes.c_void_p, ctypes.c_int, _I64x4, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _I64x4,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "qflash_fwd_fused_noalloc": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, _I64x4, _I64x4, _I64x4,
         ctypes.c_void_p, ctypes.c_int, _I64x4, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -120,6 +126,23 @@ def fwd_fused(q, k, v, mask, mask_strides, mask_zb, mask_hb, mask_z_period, q8, 
                               Z, H, N, D, scale_log2e, l_shift, acc_shift, flags,
                               workspace.data_ptr(), workspace.numel(), stream)
     _check(rc, "qflash_fwd_fused")
+
+
+def fwd_fused_out(q, k, v, mask, mask_strides, mask_zb, mask_hb, mask_z_period, q8, k8, v8, out,
+                  scale_log2e, l_shift, acc_shift, flags, workspace, stream) -> None:
+    """Launch qflash_fwd_fused_out: the epilogue writes ``out`` (any strides,
+    head dim contiguous) directly; no synchronisation."""
+    lib = load()
+    Z, H, N, D = q.shape
+    ms = (ctypes.c_int64 * 4)(*mask_strides) if mask is not None else None
+    rc = lib.qflash_fwd_fused_out(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPES[str(q.dtype)],
+                                  _strides(q), _strides(k), _strides(v),
+                                  mask.data_ptr() if mask is not None else None,
+                                  DTYPES[str(mask.dtype)] if mask is not None else -1, ms, mask_zb, mask_hb,
+                                  mask_z_period, q8.data_ptr(), k8.data_ptr(), v8.data_ptr(), out.data_ptr(),
+                                  _strides(out), Z, H, N, D, scale_log2e, l_shift, acc_shift, flags,
+                                  workspace.data_ptr(), workspace.numel(), stream)
+    _check(rc, "qflash_fwd_fused_out")
 
 
 def fused_workspace_bytes(mask_zb: int, mask_hb: int, N: int) -> int:

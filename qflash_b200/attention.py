@@ -11,6 +11,7 @@ from typing import Dict, Optional
 import torch
 from torch import nn
 
+from . import kernel as K
 from .kernel import qflash, window_attention
 from .swin import relative_position_index
 
@@ -43,6 +44,12 @@ class QAttention(nn.Module):
         B, N, C = x.shape
         qkv = self.qkv(x).reshape(B, N, 3, self.num_heads, self.head_dim).permute(2, 0, 3, 1, 4)
         q, k, v = qkv.unbind(0)
+        if K.FUSED and attn_mask is None and x.is_cuda:
+            # the attention epilogue writes [B, N, H, D] directly: the reshape
+            # below is then a view instead of a transpose copy
+            out = torch.empty((B, N, self.num_heads, self.head_dim), dtype=q.dtype, device=x.device)
+            K.forward_fused(q, k, v, out=out.permute(0, 2, 1, 3))
+            return self.proj(out.reshape(B, N, C))
         x = qflash.forward(q, k, v, attn_mask=attn_mask)
         return self.proj(x.transpose(1, 2).reshape(B, N, C))
 

@@ -5,6 +5,23 @@
 
 namespace qfb {
 
+// element types of float tensors at the boundary (and the mask's bool)
+enum : int { kF32 = 0, kF16 = 1, kBF16 = 2, kBool = 3 };
+
+// int64 slots of the device parameter block written by the on-device
+// parameter kernel (qflash_quant.cu) and read by the attention kernel
+enum : int { P_STATUS = 0, P_RS = 1, P_EM = 2, P_RM = 3, P_LM = 4, P_ACCM = 5, P_MLIM = 6, P_SM = 8, P_QS = 9,
+             P_KS = 10, P_OS = 11, P_INVSM = 12 };
+
+// Dequantised output written by the attention epilogue instead of int8 O:
+// out = int8(acc / l) * o_scale in `dtype` (kF32 / kF16 / kBF16) at element
+// `strides`, o_scale taken from the device parameter block (P_OS).
+struct OutSpec {
+  void* p;
+  int dtype;
+  int64_t strides[4];
+};
+
 int set_err(int code, const char* fmt, ...);
 int select_device(const void* p, int* dev);
 int sm_count(int dev);
@@ -15,7 +32,7 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
                   const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
                   const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N,
                   int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
-                  int32_t acc_shift, uint32_t flags, const long long* dparams, void* stream);
+                  int32_t acc_shift, uint32_t flags, const long long* dparams, const OutSpec* out, void* stream);
 
 
 // The on-device forward behind qflash_fwd_fused and the workspace it needs.
@@ -23,7 +40,8 @@ size_t fused_workspace_bytes(int bias_zb, int bias_hb, int N);
 int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
               const int64_t k_strides[4], const int64_t v_strides[4], const void* mask, int mask_dtype,
               const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period, int8_t* q8, int8_t* k8,
-              int8_t* v8, int8_t* o8, void* out, int Z, int H, int N, int D, double scale_log2e, int32_t l_shift,
-              int32_t acc_shift, uint32_t flags, void* ws, size_t ws_bytes, void* stream);
+              int8_t* v8, int8_t* o8, void* out, const int64_t out_strides[4], int Z, int H, int N, int D,
+              double scale_log2e, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* ws, size_t ws_bytes,
+              void* stream);
 
 }  // namespace qfb

@@ -21,6 +21,8 @@
 // The MMA warp issues S_{g+1} before PV_g, so the tensor core computes the
 // next scores while the softmax warps work on the current chunk.
 #include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -33,6 +35,7 @@
 #include <string>
 
 #include "../../include/qflash_b200.h"
+#include "qfb_internal.h"
 #include "sm100_ptx.cuh"
 
 namespace qfb {
@@ -65,8 +68,14 @@ struct KArgs {
   int m_lim;
   // When set, the fixed-point constants come from device memory (written by
   // the on-device parameter kernel): [0] status (non-zero: do nothing),
-  // [1] sm_rscale [2] exp_M [3] req_M [4] l_M [5] acc_M [6] m_lim.
+  // [1] sm_rscale [2] exp_M [3] req_M [4] l_M [5] acc_M [6] m_lim, [11] o_scale.
   const long long* dparams;
+  // When set (with dparams), the epilogue writes int8(acc / l) * o_scale in
+  // out_dtype at these element strides instead of int8 O.
+  void* out;
+  long long ou_z, ou_h, ou_n;
+  int out_dtype, out_vec16;
+  float o_scale;
 };
 
 // ------------------------------------------------------------------ integer primitives
@@ -152,6 +161,49 @@ __device__ __forceinline__ int div_to_i32(int acc, int l, bool full) {
   return (qf >= -2147483648.0f && qf < 2147483648.0f) ? __float2int_rz(qf) : (int)0x80000000;
 }
 
+// 32 int8 values (packed four per word) times o_scale, rounded to the output
+// dtype, stored at dst: o * o_scale as torch evaluates it (qflash/kernel.py:351),
+// the product in fp32 and one rounding to the dtype.
+__device__ __forceinline__ void store_dequant32(void* dst, const uint32_t (&res)[8], float os, int dtype, bool vec16) {
+  float f[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) f[i] = (float)(int8_t)(res[i >> 2] >> (8 * (i & 3))) * os;
+  if (dtype == kF32) {
+    float* d = (float*)dst;
+    if (vec16) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) *(float4*)(d + 4 * i) = make_float4(f[4 * i], f[4 * i + 1], f[4 * i + 2], f[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) d[i] = f[i];
+    }
+  } else {
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (dtype == kF16) {
+        const __half2 h2 = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *(const uint32_t*)&h2;
+      } else {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *(const uint32_t*)&b2;
+      }
+    }
+    if (vec16) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        *(uint4*)((uint8_t*)dst + 16 * i) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    } else {
+      uint16_t* d = (uint16_t*)dst;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        d[2 * i] = (uint16_t)w[i];
+        d[2 * i + 1] = (uint16_t)(w[i] >> 16);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 // SEGS = 2 packs two heads (of N <= 64 rows each) into one 128-row tile:
 // rows [0, 64) belong to head 2*item, rows [64, 128) to head 2*item + 1.
@@ -215,6 +267,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     a.lM = dp[4];
     a.accM = dp[5];
     a.m_lim = (int)dp[6];
+    a.o_scale = __int_as_float((int)dp[P_OS]);
   }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -660,7 +713,13 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
               res[7] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
             }
           }
-          if (row_ok) {
+          if (row_ok && a.out) {
+            const int esz = a.out_dtype == kF32 ? 4 : 2;
+            uint8_t* drow = (uint8_t*)a.out +
+                            ((long long)z * a.ou_z + (long long)h * a.ou_h + (long long)row * a.ou_n + a.v_col0 +
+                             part * 32) * esz;
+            store_dequant32(drow, res, a.o_scale, a.out_dtype, a.out_vec16);
+          } else if (row_ok) {
             if (a.o_vec16) {
               *(int4*)(orow + part * 32) = make_int4((int)res[0], (int)res[1], (int)res[2], (int)res[3]);
               *(int4*)(orow + part * 32 + 16) = make_int4((int)res[4], (int)res[5], (int)res[6], (int)res[7]);
@@ -825,14 +884,17 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
                   const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
                   const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N,
                   int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
-                  int32_t acc_shift, uint32_t flags, const long long* dparams, void* stream_) {
+                  int32_t acc_shift, uint32_t flags, const long long* dparams, const OutSpec* out, void* stream_) {
   cudaStream_t stream = (cudaStream_t)stream_;
   if (Z < 0 || H < 0 || N < 0) return set_err(QFLASH_ERR_ARG, "negative shape");
   if (!(D == 32 || D == 64 || D == 128 || D == 256)) return set_err(QFLASH_ERR_ARG, "head dim %d not in {32,64,128,256}", D);
   if (Z == 0 || H == 0 || N == 0) return QFLASH_OK;
-  if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides)
+  const bool fused_out = out != nullptr;
+  if (fused_out && (!dparams || !out->p || out->dtype < kF32 || out->dtype > kBF16 || out->strides[3] != 1))
+    return set_err(QFLASH_ERR_ARG, "dequantised output needs device constants, a float dtype and a contiguous head dim");
+  if (!q || !k || !v || !q_strides || !k_strides || !v_strides || (!fused_out && (!o || !o_strides)))
     return set_err(QFLASH_ERR_ARG, "null pointer");
-  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || o_strides[3] != 1)
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || (!fused_out && o_strides[3] != 1))
     return set_err(QFLASH_ERR_ARG, "innermost (head-dim) stride must be 1");
   if (!dparams && sm_rscale <= 0) return set_err(QFLASH_ERR_ARG, "sm_rscale must be positive");
   if (l_shift < 1 || l_shift > 62 || acc_shift < 1 || acc_shift > 62) return set_err(QFLASH_ERR_ARG, "shift out of [1, 62]");
@@ -857,12 +919,23 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
   ka.bias_zmod = bias_z_period;
   if (items > 0x7fffffffLL) return set_err(QFLASH_ERR_ARG, "too many tiles");
   ka.nitems = (int)items;
-  ka.o = o;
-  ka.os_z = o_strides[0];
-  ka.os_h = o_strides[1];
-  ka.os_n = o_strides[2];
-  ka.o_vec16 = (((uintptr_t)o & 15) == 0) && (o_strides[0] % 16 == 0) && (o_strides[1] % 16 == 0) &&
-               (o_strides[2] % 16 == 0);
+  if (fused_out) {
+    const int esz = out->dtype == kF32 ? 4 : 2;
+    ka.out = out->p;
+    ka.out_dtype = out->dtype;
+    ka.ou_z = out->strides[0];
+    ka.ou_h = out->strides[1];
+    ka.ou_n = out->strides[2];
+    ka.out_vec16 = (((uintptr_t)out->p & 15) == 0) && (out->strides[0] * esz % 16 == 0) &&
+                   (out->strides[1] * esz % 16 == 0) && (out->strides[2] * esz % 16 == 0);
+  } else {
+    ka.o = o;
+    ka.os_z = o_strides[0];
+    ka.os_h = o_strides[1];
+    ka.os_n = o_strides[2];
+    ka.o_vec16 = (((uintptr_t)o & 15) == 0) && (o_strides[0] % 16 == 0) && (o_strides[1] % 16 == 0) &&
+                 (o_strides[2] % 16 == 0);
+  }
   ka.rs = sm_rscale;
   ka.eM = exp_M;
   ka.rM = req_M;
@@ -968,7 +1041,7 @@ extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* 
                                 int64_t acc_M, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream) {
   return qfb::attention_fwd(q, k, v, o, bias, q_strides, k_strides, v_strides, o_strides, bias_strides,
                             bias_z_period, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags,
-                            nullptr, stream);
+                            nullptr, nullptr, stream);
 }
 
 extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,

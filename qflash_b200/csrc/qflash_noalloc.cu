@@ -65,7 +65,8 @@ extern "C" int qflash_fwd_fused_noalloc(const void* q, const void* k, const void
   if (dev >= qfb::kMaxDevs) return qfb::set_err(QFLASH_ERR_DEVICE, "device %d", dev);
   void* ws = nullptr;
   if (int rc = qfb::scratch_on(dev, &ws)) return rc;
+  if (!o8) return qfb::set_err(QFLASH_ERR_ARG, "null pointer");
   return qfb::fused_fwd(q, k, v, dtype, q_strides, k_strides, v_strides, mask, mask_dtype, mask_strides, mask_zb,
-                        mask_hb, mask_z_period, q8, k8, v8, o8, out, Z, H, N, D, scale_log2e, l_shift, acc_shift,
-                        flags, ws, qfb::kNoAllocScratchBytes, stream);
+                        mask_hb, mask_z_period, q8, k8, v8, o8, out, nullptr, Z, H, N, D, scale_log2e, l_shift,
+                        acc_shift, flags, ws, qfb::kNoAllocScratchBytes, stream);
 }

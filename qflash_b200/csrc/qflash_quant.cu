@@ -29,11 +29,6 @@
 
 namespace qfb {
 
-enum : int { kF32 = 0, kF16 = 1, kBF16 = 2, kBool = 3 };
-
-// params block (int64 slots) written by params_kernel, read by the others
-enum : int { P_STATUS = 0, P_RS = 1, P_EM = 2, P_RM = 3, P_LM = 4, P_ACCM = 5, P_MLIM = 6, P_SM = 8, P_QS = 9,
-             P_KS = 10, P_OS = 11, P_INVSM = 12 };
 constexpr int kParamsBytes = 256;
 constexpr int kMaxPartials = 1024;  // blocks of the |max| reduction
 constexpr int kNegInfI = -(1 << 20);
@@ -96,6 +91,110 @@ __global__ void amax3_kernel(Rows q, Rows k, Rows v, int H, int N, int D, int nr
     float mm = sm[0];
     for (int i = 1; i < wpb; ++i) mm = nmax(mm, sm[i]);
     partials[blockIdx.y * gridDim.x + blockIdx.x] = mm;
+  }
+}
+
+// ---- vectorised forms: one thread per 16-byte vector of a row (rows 16-byte
+// aligned; D * element size is a power of two >= 64, so vectors per row are too)
+template <int T>
+constexpr int kVecElems = T == kF32 ? 4 : 8;
+
+// element e (0 .. kVecElems - 1) of a 16-byte vector as float
+template <int T>
+__device__ __forceinline__ float vec_elem(const uint4& u, int e) {
+  if constexpr (T == kF32) {
+    const uint32_t x = e == 0 ? u.x : (e == 1 ? u.y : (e == 2 ? u.z : u.w));
+    return __int_as_float((int)x);
+  } else {
+    const uint32_t x = (e >> 1) == 0 ? u.x : ((e >> 1) == 1 ? u.y : ((e >> 1) == 2 ? u.z : u.w));
+    const uint16_t b = (uint16_t)(x >> (16 * (e & 1)));
+    if constexpr (T == kF16) return __half2float(__ushort_as_half(b));
+    else return __bfloat162float(__ushort_as_bfloat16(b));
+  }
+}
+
+// element offset of vector i of a [Z, H, N, D] strided tensor (vpr = 1 << vshift vectors per row)
+__device__ __forceinline__ long long vec_offset(const Rows& r, unsigned i, int vshift, int H, int N, int ve) {
+  const unsigned row = i >> vshift, cv = i & ((1u << vshift) - 1);
+  const unsigned c = row % (unsigned)N, t = row / (unsigned)N, b = t % (unsigned)H, a = t / (unsigned)H;
+  return (long long)a * r.s0 + (long long)b * r.s1 + (long long)c * r.s2 + (long long)cv * ve;
+}
+
+template <int T>
+__global__ void amax3v_kernel(Rows q, Rows k, Rows v, int H, int N, int vshift, unsigned nvec, float* partials) {
+  using E = Elt<T>;
+  constexpr int VE = kVecElems<T>;
+  const Rows r = blockIdx.y == 0 ? q : (blockIdx.y == 1 ? k : v);
+  const typename E::type* x = (const typename E::type*)r.p;
+  float m = 0.f;
+  // four vectors in flight per thread
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < nvec; i0 += 4 * stride) {
+    uint4 u[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const unsigned i = i0 + j * stride;
+      u[j] = i < nvec ? __ldg((const uint4*)(x + vec_offset(r, i, vshift, H, N, VE))) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < VE; ++e) m = nmax(m, fabsf(vec_elem<T>(u[j], e)));
+  }
+  for (int o = 16; o; o >>= 1) m = nmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float sm[32];
+  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = sm[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) mm = nmax(mm, sm[i]);
+    partials[blockIdx.y * gridDim.x + blockIdx.x] = mm;
+  }
+}
+
+template <int T>
+__global__ void quantize3v_kernel(Rows q, Rows k, Rows v, int H, int N, int D, int vshift, unsigned nvec,
+                                  const long long* dp, int8_t* q8, int8_t* k8, int8_t* v8) {
+  using E = Elt<T>;
+  constexpr int VE = kVecElems<T>;
+  if (dp[P_STATUS] != 0) return;
+  const int t = blockIdx.y;
+  const Rows r = t == 0 ? q : (t == 1 ? k : v);
+  int8_t* out = t == 0 ? q8 : (t == 1 ? k8 : v8);
+  const float s = __int_as_float((int)dp[P_QS + t]);
+  const typename E::type* x = (const typename E::type*)r.p;
+  // x / s: for 16-bit inputs with s in [2^-96, 2^96] as RN(x * RN(1/s)) plus one
+  // FMA residual step, which equals the IEEE quotient for every 16-bit x with
+  // 1/16 <= |x / s| <= 256 (checked exhaustively over all fp16 and bf16 pairs);
+  // smaller quotients round to 0 either way and |x| <= amax bounds |x / s| by
+  // about 127.  Otherwise the IEEE division.
+  const bool fastdiv = T != kF32 && s >= 1.2621774e-29f && s <= 7.9228163e+28f;
+  const float R = __frcp_rn(s);
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += gridDim.x * blockDim.x) {
+    const uint4 u = __ldg((const uint4*)(x + vec_offset(r, i, vshift, H, N, VE)));
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      const float xe = vec_elem<T>(u, e);
+      float q;
+      if (fastdiv) {
+        const float q0 = __fmul_rn(xe, R);
+        q = __fmaf_rn(__fmaf_rn(-q0, s, xe), R, q0);
+      } else {
+        q = __fdiv_rn(xe, s);
+      }
+      const float y = rt<T>(q);
+      // clamp(round(y)) == round(clamp(y)) for round-half-even; the 1.5 * 2^23
+      // add rounds to an integer; NaN gives 0 like the float -> int8 conversion
+      const float c = fminf(fmaxf(y, -128.f), 127.f);
+      const int v8 = y != y ? 0 : __float_as_int(__fadd_rn(c, 12582912.f)) - 0x4B400000;
+      packed[e >> 2] |= (uint32_t)(v8 & 0xff) << (8 * (e & 3));
+    }
+    // the int8 output is contiguous: vector i covers bytes [i * VE, i * VE + VE)
+    int8_t* o = out + (long long)i * VE;
+    if constexpr (VE == 8) *(uint2*)o = make_uint2(packed[0], packed[1]);
+    else *(uint32_t*)o = packed[0];
+    (void)D;
   }
 }
 
@@ -249,18 +348,40 @@ size_t fused_workspace_bytes(int bias_zb, int bias_hb, int N) {
 }
 
 // The fused forward; `ws` is device memory of at least fused_workspace_bytes().
+// NaN into every element of a strided output when the constants could not be
+// formed (the attention kernel then wrote nothing); does nothing otherwise
+template <int T>
+__global__ void nan_fill_kernel(void* out, long long s0, long long s1, long long s2, int H, int N, int D, long long n,
+                                const long long* dp) {
+  if (dp[P_STATUS] == 0) return;
+  using E = Elt<T>;
+  typename E::type* y = (typename E::type*)out;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / D, d = i - r * D;
+    const long long t = r / N, c = r - t * N;
+    const long long a = t / H, b = t - a * H;
+    y[a * s0 + b * s1 + c * s2 + d] = E::t(__int_as_float(0x7fc00000));
+  }
+}
+
 int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
               const int64_t k_strides[4], const int64_t v_strides[4], const void* mask, int mask_dtype,
               const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period, int8_t* q8, int8_t* k8,
-              int8_t* v8, int8_t* o8, void* out, int Z, int H, int N, int D, double scale_log2e, int32_t l_shift,
-              int32_t acc_shift, uint32_t flags, void* ws, size_t ws_bytes, void* stream_) {
+              int8_t* v8, int8_t* o8, void* out, const int64_t out_strides[4], int Z, int H, int N, int D,
+              double scale_log2e, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* ws, size_t ws_bytes,
+              void* stream_) {
   cudaStream_t stream = (cudaStream_t)stream_;
   if (Z < 0 || H < 0 || N < 0) return set_err(QFLASH_ERR_ARG, "negative shape");
   if (!(D == 32 || D == 64 || D == 128 || D == 256)) return set_err(QFLASH_ERR_ARG, "head dim %d not in {32,64,128,256}", D);
   if (dtype < kF32 || dtype > kBF16) return set_err(QFLASH_ERR_ARG, "dtype %d not in {0 f32, 1 f16, 2 bf16}", dtype);
   if (Z == 0 || H == 0 || N == 0) return QFLASH_OK;
-  if (!q || !k || !v || !q8 || !k8 || !v8 || !o8 || !out || !ws || !q_strides || !k_strides || !v_strides)
+  // without o8 the attention epilogue writes `out` itself (at out_strides, or contiguous)
+  if (!q || !k || !v || !q8 || !k8 || !v8 || !out || !ws || !q_strides || !k_strides || !v_strides)
     return set_err(QFLASH_ERR_ARG, "null pointer");
+  if (o8 && out_strides && !(out_strides[3] == 1 && out_strides[2] == D && out_strides[1] == (int64_t)N * D &&
+                             out_strides[0] == (int64_t)H * N * D))
+    return set_err(QFLASH_ERR_ARG, "with o8 the output must be contiguous");
+  if (out_strides && out_strides[3] != 1) return set_err(QFLASH_ERR_ARG, "output head-dim stride must be 1");
   if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1)
     return set_err(QFLASH_ERR_ARG, "innermost (head-dim) stride must be 1");
   if (l_shift < 1 || l_shift > 62 || acc_shift < 1 || acc_shift > 62) return set_err(QFLASH_ERR_ARG, "shift out of [1, 62]");
@@ -294,7 +415,39 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
   P = P < kMaxPartials ? P : kMaxPartials;
   const dim3 g3(P, 3);
   const double sl = scale_log2e;
-  switch (dtype) {
+  // 16-byte vectors per row when every row of Q, K, V starts 16-byte aligned
+  const int esz = dtype == kF32 ? 4 : 2;
+  auto aligned = [&](const Rows& r) {
+    return ((uintptr_t)r.p & 15) == 0 && (r.s0 * esz) % 16 == 0 && (r.s1 * esz) % 16 == 0 && (r.s2 * esz) % 16 == 0;
+  };
+  const long long nvec_ll = (long long)nrows * D * esz / 16;
+  if (aligned(rq) && aligned(rk) && aligned(rv) && nvec_ll < (1ll << 31)) {
+    const unsigned nvec = (unsigned)nvec_ll;
+    int vshift = 0;
+    while ((1 << vshift) < D * esz / 16) ++vshift;
+    int PV = (int)((nvec + 255) / 256);
+    const int capv = 4 * sm_count(dev);
+    PV = PV < capv ? PV : capv;
+    PV = PV < kMaxPartials ? PV : kMaxPartials;
+    const dim3 gv(PV, 3);
+    switch (dtype) {
+      case kF32:
+        amax3v_kernel<kF32><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, vshift, nvec, partials);
+        params_kernel<kF32><<<1, 256, 0, stream>>>(partials, PV, sl, l_shift, acc_shift, D, dp);
+        quantize3v_kernel<kF32><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, dp, q8, k8, v8);
+        break;
+      case kF16:
+        amax3v_kernel<kF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, vshift, nvec, partials);
+        params_kernel<kF16><<<1, 256, 0, stream>>>(partials, PV, sl, l_shift, acc_shift, D, dp);
+        quantize3v_kernel<kF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, dp, q8, k8, v8);
+        break;
+      default:
+        amax3v_kernel<kBF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, vshift, nvec, partials);
+        params_kernel<kBF16><<<1, 256, 0, stream>>>(partials, PV, sl, l_shift, acc_shift, D, dp);
+        quantize3v_kernel<kBF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, dp, q8, k8, v8);
+        break;
+    }
+  } else switch (dtype) {
     case kF32:
       amax3_kernel<kF32><<<g3, threads, 0, stream>>>(rq, rk, rv, H, N, D, nrows, partials);
       params_kernel<kF32><<<1, 256, 0, stream>>>(partials, P, sl, l_shift, acc_shift, D, dp);
@@ -338,11 +491,36 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "quantisation launch: %s", cudaGetErrorString(e));
   const int64_t st8[4] = {(int64_t)H * N * D, (int64_t)N * D, D, 1};
+  const long long n = (long long)nrows * D;
+  if (!o8) {
+    OutSpec os;
+    os.p = out;
+    os.dtype = dtype;
+    for (int i = 0; i < 4; ++i) os.strides[i] = out_strides ? out_strides[i] : st8[i];
+    int rc = attention_fwd(q8, k8, v8, nullptr, has_mask ? bias : nullptr, st8, st8, st8, nullptr,
+                           has_mask ? bstr : nullptr, has_mask ? mask_z_period : 0, Z, H, N, D, 0, 0, 0, 0, 0, l_shift,
+                           acc_shift, flags, dp, &os, stream);
+    if (rc) return rc;
+    const int ngrid = sm_count(dev);
+    switch (dtype) {
+      case kF32:
+        nan_fill_kernel<kF32><<<ngrid, 256, 0, stream>>>(out, os.strides[0], os.strides[1], os.strides[2], H, N, D, n, dp);
+        break;
+      case kF16:
+        nan_fill_kernel<kF16><<<ngrid, 256, 0, stream>>>(out, os.strides[0], os.strides[1], os.strides[2], H, N, D, n, dp);
+        break;
+      default:
+        nan_fill_kernel<kBF16><<<ngrid, 256, 0, stream>>>(out, os.strides[0], os.strides[1], os.strides[2], H, N, D, n, dp);
+        break;
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "output launch: %s", cudaGetErrorString(e));
+    return QFLASH_OK;
+  }
   int rc = attention_fwd(q8, k8, v8, o8, has_mask ? bias : nullptr, st8, st8, st8, st8, has_mask ? bstr : nullptr,
                          has_mask ? mask_z_period : 0, Z, H, N, D, 0, 0, 0, 0, 0, l_shift, acc_shift, flags, dp,
-                         stream);
+                         nullptr, stream);
   if (rc) return rc;
-  const long long n = (long long)nrows * D;
   const int dgrid = cap * 4;
   switch (dtype) {
     case kF32: dequant_kernel<kF32><<<dgrid, 256, 0, stream>>>(o8, n, dp, out); break;
@@ -366,9 +544,22 @@ extern "C" int qflash_fwd_fused(const void* q, const void* k, const void* v, int
                                 int mask_z_period, int8_t* q8, int8_t* k8, int8_t* v8, int8_t* o8, void* out, int Z,
                                 int H, int N, int D, double scale_log2e, int32_t l_shift, int32_t acc_shift,
                                 uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!o8) return qfb::set_err(QFLASH_ERR_ARG, "null pointer");
   return qfb::fused_fwd(q, k, v, dtype, q_strides, k_strides, v_strides, mask, mask_dtype, mask_strides, mask_zb,
-                        mask_hb, mask_z_period, q8, k8, v8, o8, out, Z, H, N, D, scale_log2e, l_shift, acc_shift,
-                        flags, workspace, workspace_bytes, stream);
+                        mask_hb, mask_z_period, q8, k8, v8, o8, out, nullptr, Z, H, N, D, scale_log2e, l_shift,
+                        acc_shift, flags, workspace, workspace_bytes, stream);
+}
+
+extern "C" int qflash_fwd_fused_out(const void* q, const void* k, const void* v, int dtype,
+                                    const int64_t q_strides[4], const int64_t k_strides[4],
+                                    const int64_t v_strides[4], const void* mask, int mask_dtype,
+                                    const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period,
+                                    int8_t* q8, int8_t* k8, int8_t* v8, void* out, const int64_t out_strides[4], int Z,
+                                    int H, int N, int D, double scale_log2e, int32_t l_shift, int32_t acc_shift,
+                                    uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
+  return qfb::fused_fwd(q, k, v, dtype, q_strides, k_strides, v_strides, mask, mask_dtype, mask_strides, mask_zb,
+                        mask_hb, mask_z_period, q8, k8, v8, nullptr, out, out_strides, Z, H, N, D, scale_log2e,
+                        l_shift, acc_shift, flags, workspace, workspace_bytes, stream);
 }
 
 extern "C" int qflash_fused_status(const void* workspace, void* stream, int64_t* status) {

@@ -182,13 +182,19 @@ def qflash_forward(
 
 
 def forward_fused(query, key, value, attn_mask=None, scale=None, bias_z_period=0, check=False,
-                  return_int8=False, return_workspace=False):
+                  return_int8=False, return_workspace=False, out=None):
     """``qflash.forward`` with every step on the device (``qflash_fwd_fused``):
     no ``.item()`` synchronisation, no torch quantisation passes.  The output
     equals ``qflash.forward``'s bit for bit (contiguous [Z, H, N, D], input
     dtype).  ``check`` synchronises and raises where the reference raises
     (ZeroDivisionError for an all-zero q or k); without it such inputs give
-    an all-NaN output.  ``bias_z_period`` as in ``forward_with_scales``."""
+    an all-NaN output.  ``bias_z_period`` as in ``forward_with_scales``.
+
+    Unless ``return_int8`` is set, the attention epilogue writes the
+    dequantised output itself (``qflash_fwd_fused_out``): into ``out`` when
+    given (a [Z, H, N, D] tensor or view of the input dtype with a contiguous
+    head dim, e.g. a permuted [Z, N, H, D] buffer), else into a new contiguous
+    tensor."""
     D = query.shape[-1]
     assert query.shape[-1] == key.shape[-1] == value.shape[-1]
     assert D in {16, 32, 64, 128, 256}
@@ -196,6 +202,9 @@ def forward_fused(query, key, value, attn_mask=None, scale=None, bias_z_period=0
         raise ValueError("head dim 16 is not supported (the chunk width 32 exceeds it), as in the reference")
     if not (query.is_cuda and key.is_cuda and value.is_cuda):
         raise ValueError("qflash.forward runs on CUDA tensors only")
+    if not (query.dim() == 4 and query.shape == key.shape == value.shape):
+        raise ValueError(f"fused path takes q, k, v of one [Z, H, N, D] shape, got "
+                         f"{tuple(query.shape)}, {tuple(key.shape)}, {tuple(value.shape)}")
     if query.dtype not in (torch.float32, torch.float16, torch.bfloat16) or not (
             query.dtype == key.dtype == value.dtype):
         raise ValueError(f"fused path takes float32/float16/bfloat16 inputs of one dtype, got {query.dtype}")
@@ -215,12 +224,23 @@ def forward_fused(query, key, value, attn_mask=None, scale=None, bias_z_period=0
         mask = m
         mstr = [0 if m.shape[i] == 1 else m.stride(i) for i in range(4)]
     dev = q.device
-    q8, k8, v8, o8 = (torch.empty((Z, H, N, D), dtype=torch.int8, device=dev) for _ in range(4))
-    out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
+    q8, k8, v8 = (torch.empty((Z, H, N, D), dtype=torch.int8, device=dev) for _ in range(3))
+    if out is None:
+        out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
+    elif out.shape != (Z, H, N, D) or out.dtype != q.dtype or out.stride(-1) != 1 or out.device != dev:
+        raise ValueError(f"out must be a {(Z, H, N, D)} {q.dtype} tensor on {dev} with a contiguous last dim")
     ws = torch.empty(_lib.fused_workspace_bytes(zb, hb, N), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    _lib.fwd_fused(q, k, v, mask, mstr, zb, hb, bias_z_period if mask is not None else 0, q8, k8, v8, o8, out,
-                   scale * LOG2E, L_SHIFT, ACC_SHIFT, arith_flags(), ws, stream)
+    period = bias_z_period if mask is not None else 0
+    if return_int8:
+        if not out.is_contiguous():
+            raise ValueError("return_int8 needs a contiguous output")
+        o8 = torch.empty((Z, H, N, D), dtype=torch.int8, device=dev)
+        _lib.fwd_fused(q, k, v, mask, mstr, zb, hb, period, q8, k8, v8, o8, out,
+                       scale * LOG2E, L_SHIFT, ACC_SHIFT, arith_flags(), ws, stream)
+    else:
+        _lib.fwd_fused_out(q, k, v, mask, mstr, zb, hb, period, q8, k8, v8, out,
+                           scale * LOG2E, L_SHIFT, ACC_SHIFT, arith_flags(), ws, stream)
     if check:
         st = _lib.fused_status(ws, stream)
         if st == 1:
