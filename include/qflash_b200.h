@@ -118,12 +118,35 @@ int qflash_fwd_fused_out(const void* q, const void* k, const void* v, int dtype,
                          double scale_log2e, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/*
+ * qflash_fwd_fused_out for Swin window attention with the bias built on the
+ * device from its parts instead of a dense float mask: entry (w, h, i, j) of
+ * the mask is table[index[i * N + j], h] plus window_mask[w, i, j] (added in
+ * the promoted dtype of the two, as QWindowAttention does at
+ * qflash/attention.py:68-72), then quantised as kernel.py:332-336 does.  The
+ * reference expands that mask to [Z, H, N, N] (118 MB of int32 bias for Swin-T
+ * stage 1); here it exists once per window and head, and batch z uses window
+ * z % num_windows.  table: [table_rows, H] of table_dtype at element strides
+ * table_strides; index: int64 [N * N] contiguous; window_mask: [num_windows, N,
+ * N] contiguous of window_mask_dtype, or NULL (bias only; num_windows ignored).
+ * Workspace: qflash_fused_workspace_bytes(window_mask ? num_windows : 1, H, N).
+ * An index outside the table gives status 3 (and a NaN output).
+ */
+int qflash_fwd_fused_window(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
+                            const int64_t k_strides[4], const int64_t v_strides[4], const void* table,
+                            int table_dtype, const int64_t table_strides[2], int table_rows, const int64_t* index,
+                            const void* window_mask, int window_mask_dtype, int num_windows, int8_t* q8, int8_t* k8,
+                            int8_t* v8, void* out, const int64_t out_strides[4], int Z, int H, int N, int D,
+                            double scale_log2e, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Workspace bytes qflash_fwd_fused needs (mask_zb = mask_hb = 0 without a mask). */
 size_t qflash_fused_workspace_bytes(int mask_zb, int mask_hb, int N);
 
 /* Synchronises the stream and reads the status the fused forward recorded in its
  * workspace: 0 ok, 1 division by zero (the reference raises ZeroDivisionError),
- * 2 constants not representable (NaN/inf scales, or beyond int32). */
+ * 2 constants not representable (NaN/inf scales, or beyond int32), 3 a window
+ * bias index outside its table. */
 int qflash_fused_status(const void* workspace, void* stream, int64_t* status);
 
 /*

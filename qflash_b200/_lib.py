@@ -47,6 +47,13 @@ SIGNATURES = {
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _I64x4,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int32, ctypes.c_int32,
         ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "qflash_fwd_fused_window": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, _I64x4, _I64x4, _I64x4,
+        ctypes.c_void_p, ctypes.c_int, ctypes.c_int64 * 2, ctypes.c_int, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _I64x4,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "qflash_fwd_fused_noalloc": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, _I64x4, _I64x4, _I64x4,
         ctypes.c_void_p, ctypes.c_int, _I64x4, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -143,6 +150,24 @@ def fwd_fused_out(q, k, v, mask, mask_strides, mask_zb, mask_hb, mask_z_period, 
                                   _strides(out), Z, H, N, D, scale_log2e, l_shift, acc_shift, flags,
                                   workspace.data_ptr(), workspace.numel(), stream)
     _check(rc, "qflash_fwd_fused_out")
+
+
+def fwd_fused_window(q, k, v, table, index, window_mask, num_windows, q8, k8, v8, out,
+                     scale_log2e, l_shift, acc_shift, flags, workspace, stream) -> None:
+    """Launch qflash_fwd_fused_window (Swin bias built on the device)."""
+    lib = load()
+    Z, H, N, D = q.shape
+    ts = (ctypes.c_int64 * 2)(int(table.stride(0)), int(table.stride(1)))
+    rc = lib.qflash_fwd_fused_window(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPES[str(q.dtype)],
+                                     _strides(q), _strides(k), _strides(v),
+                                     table.data_ptr(), DTYPES[str(table.dtype)], ts, int(table.shape[0]),
+                                     index.data_ptr(),
+                                     window_mask.data_ptr() if window_mask is not None else None,
+                                     DTYPES[str(window_mask.dtype)] if window_mask is not None else -1,
+                                     num_windows, q8.data_ptr(), k8.data_ptr(), v8.data_ptr(), out.data_ptr(),
+                                     _strides(out), Z, H, N, D, scale_log2e, l_shift, acc_shift, flags,
+                                     workspace.data_ptr(), workspace.numel(), stream)
+    _check(rc, "qflash_fwd_fused_window")
 
 
 def fused_workspace_bytes(mask_zb: int, mask_hb: int, N: int) -> int:

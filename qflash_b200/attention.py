@@ -96,8 +96,15 @@ class QWindowAttention(nn.Module):
         q, k, v = qkv.unbind(0)
 
         # the reference adds the (window) mask to the bias at full batch size and
-        # calls qflash.forward(q, k, v, attn_mask=...); window_attention gives the
-        # same result from the per-window bias (see its docstring)
+        # calls qflash.forward(q, k, v, attn_mask=...); the per-window forms below
+        # give the same result (see their docstrings)
+        if K.FUSED and x.is_cuda and q.dtype in (torch.float32, torch.float16, torch.bfloat16):
+            # bias built on the device from table, index and mask; output written
+            # in the [B_, N, H, D] layout the reshape below takes as a view
+            out = torch.empty((B_, N, self.num_heads, q.shape[-1]), dtype=q.dtype, device=x.device)
+            K.forward_window_fused(q, k, v, self.relative_position_bias_table, self.relative_position_index,
+                                   mask, out=out.permute(0, 2, 1, 3))
+            return self.proj(out.reshape(B_, N, -1))
         x = window_attention(q, k, v, self._get_rel_pos_bias(), mask)
         return self.proj(x.transpose(1, 2).reshape(B_, N, -1))
 

@@ -22,6 +22,20 @@ struct OutSpec {
   int64_t strides[4];
 };
 
+// Swin window bias built on the device (qflash/attention.py:58-76): entry
+// (w, h, i, j) of the float mask is table[index[i * N + j], h] (+ mask[w, i, j]
+// when a window mask is given, added in the promoted dtype of the two).
+struct WindowBiasSpec {
+  const void* table;
+  int table_dtype;
+  int64_t table_strides[2];
+  int table_rows;
+  const int64_t* index;  // [N * N], contiguous
+  const void* mask;      // [nW, N, N] contiguous, or null
+  int mask_dtype;
+  int num_windows;
+};
+
 int set_err(int code, const char* fmt, ...);
 int select_device(const void* p, int* dev);
 int sm_count(int dev);
@@ -42,6 +56,6 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
               const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period, int8_t* q8, int8_t* k8,
               int8_t* v8, int8_t* o8, void* out, const int64_t out_strides[4], int Z, int H, int N, int D,
               double scale_log2e, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* ws, size_t ws_bytes,
-              void* stream);
+              void* stream, const WindowBiasSpec* wb = nullptr);
 
 }  // namespace qfb

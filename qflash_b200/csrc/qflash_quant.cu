@@ -348,6 +348,50 @@ size_t fused_workspace_bytes(int bias_zb, int bias_hb, int N) {
 }
 
 // The fused forward; `ws` is device memory of at least fused_workspace_bytes().
+__device__ __forceinline__ float load_any(const void* p, long long i, int dt) {
+  if (dt == kF32) return ((const float*)p)[i];
+  if (dt == kF16) return __half2float(((const __half*)p)[i]);
+  return __bfloat162float(((const __nv_bfloat16*)p)[i]);
+}
+__device__ __forceinline__ float round_any(float x, int dt) {
+  if (dt == kF16) return rt<kF16>(x);
+  if (dt == kBF16) return rt<kBF16>(x);
+  return x;
+}
+
+// The Swin window bias: the float mask entry from the table (plus the window
+// mask), then the bias quantisation of bias_kernel in the mask's dtype, into
+// [Zb, H, N, N4] with Zb = nW (or 1 without a window mask).  An index outside
+// the table sets status 3 and is not read.
+__global__ void window_bias_kernel(WindowBiasSpec wb, int H, int N, int N4, int nrows, long long* dp,
+                                   int32_t* bias) {
+  if (dp[P_STATUS] != 0) return;
+  const float inv = __int_as_float((int)dp[P_INVSM]);
+  const float log2e = 1.44269504f;
+  const int rdt = !wb.mask || wb.mask_dtype == wb.table_dtype ? wb.table_dtype : kF32;  // promoted dtype
+  for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < nrows;
+       row += gridDim.x * (blockDim.x >> 5)) {
+    const int i = row % N, t = row / N, h = t % H, w = t / H;
+    int32_t* o = bias + (long long)row * N4;
+    for (int j = threadIdx.x & 31; j < N; j += 32) {
+      const long long idx = wb.index[(long long)i * N + j];
+      if (idx < 0 || idx >= wb.table_rows) {
+        dp[P_STATUS] = 3;
+        o[j] = 0;
+        continue;
+      }
+      float a = load_any(wb.table, idx * wb.table_strides[0] + (long long)h * wb.table_strides[1], wb.table_dtype);
+      if (wb.mask) a = round_any(a + load_any(wb.mask, ((long long)w * N + i) * N + j, wb.mask_dtype), rdt);
+      const bool masked = a < -100.0f;
+      const float c = masked ? 0.0f : a;
+      const float t1 = round_any(__fmul_rn(c, log2e), rdt);
+      const float t2 = round_any(__fmul_rn(t1, inv), rdt);
+      const float rr = round_any(rintf(t2), rdt);
+      o[j] = masked ? kNegInfI : __float2int_rz(rr);
+    }
+  }
+}
+
 // NaN into every element of a strided output when the constants could not be
 // formed (the attention kernel then wrote nothing); does nothing otherwise
 template <int T>
@@ -369,7 +413,7 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
               const int64_t mask_strides[4], int mask_zb, int mask_hb, int mask_z_period, int8_t* q8, int8_t* k8,
               int8_t* v8, int8_t* o8, void* out, const int64_t out_strides[4], int Z, int H, int N, int D,
               double scale_log2e, int32_t l_shift, int32_t acc_shift, uint32_t flags, void* ws, size_t ws_bytes,
-              void* stream_) {
+              void* stream_, const WindowBiasSpec* wb) {
   cudaStream_t stream = (cudaStream_t)stream_;
   if (Z < 0 || H < 0 || N < 0) return set_err(QFLASH_ERR_ARG, "negative shape");
   if (!(D == 32 || D == 64 || D == 128 || D == 256)) return set_err(QFLASH_ERR_ARG, "head dim %d not in {32,64,128,256}", D);
@@ -385,8 +429,18 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
   if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1)
     return set_err(QFLASH_ERR_ARG, "innermost (head-dim) stride must be 1");
   if (l_shift < 1 || l_shift > 62 || acc_shift < 1 || acc_shift > 62) return set_err(QFLASH_ERR_ARG, "shift out of [1, 62]");
-  const bool has_mask = mask != nullptr;
-  if (has_mask) {
+  if (wb) {
+    // the window bias replaces a dense mask: [nW, H, N, N] with period nW, or [1, H, N, N]
+    if (mask) return set_err(QFLASH_ERR_ARG, "a dense mask and a window bias at once");
+    if (!wb->table || !wb->index || wb->table_rows < 1 || wb->table_dtype < kF32 || wb->table_dtype > kBF16 ||
+        (wb->mask && (wb->mask_dtype < kF32 || wb->mask_dtype > kBF16 || wb->num_windows < 1 || Z % wb->num_windows)))
+      return set_err(QFLASH_ERR_ARG, "window bias: table, index, float dtypes and a window count dividing Z=%d", Z);
+    mask_zb = wb->mask ? wb->num_windows : 1;
+    mask_hb = H;
+    mask_z_period = wb->mask ? wb->num_windows : 0;
+  }
+  const bool has_mask = mask != nullptr || wb != nullptr;
+  if (has_mask && !wb) {
     if (mask_dtype < kF32 || mask_dtype > kBool) return set_err(QFLASH_ERR_ARG, "mask dtype %d", mask_dtype);
     if (!mask_strides || mask_zb < 1 || mask_hb < 1 || (mask_hb != 1 && mask_hb != H))
       return set_err(QFLASH_ERR_ARG, "mask must broadcast to [Z, H, N, N]");
@@ -470,7 +524,9 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
     const int brows = mask_zb * mask_hb * N;
     const int bgrid = (brows + wpb - 1) / wpb < cap ? (brows + wpb - 1) / wpb : cap;
     const int64_t* ms = mask_strides;
-    switch (mask_dtype) {
+    if (wb) {
+      window_bias_kernel<<<bgrid, threads, 0, stream>>>(*wb, H, N, N4, brows, dp, bias);
+    } else switch (mask_dtype) {
       case kF32:
         bias_kernel<kF32><<<bgrid, threads, 0, stream>>>(mask, ms[0], ms[1], ms[2], ms[3], mask_hb, N, N4, brows, dp, bias);
         break;
@@ -560,6 +616,30 @@ extern "C" int qflash_fwd_fused_out(const void* q, const void* k, const void* v,
   return qfb::fused_fwd(q, k, v, dtype, q_strides, k_strides, v_strides, mask, mask_dtype, mask_strides, mask_zb,
                         mask_hb, mask_z_period, q8, k8, v8, nullptr, out, out_strides, Z, H, N, D, scale_log2e,
                         l_shift, acc_shift, flags, workspace, workspace_bytes, stream);
+}
+
+extern "C" int qflash_fwd_fused_window(const void* q, const void* k, const void* v, int dtype,
+                                       const int64_t q_strides[4], const int64_t k_strides[4],
+                                       const int64_t v_strides[4], const void* table, int table_dtype,
+                                       const int64_t table_strides[2], int table_rows, const int64_t* index,
+                                       const void* window_mask, int window_mask_dtype, int num_windows, int8_t* q8,
+                                       int8_t* k8, int8_t* v8, void* out, const int64_t out_strides[4], int Z, int H,
+                                       int N, int D, double scale_log2e, int32_t l_shift, int32_t acc_shift,
+                                       uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!table_strides) return qfb::set_err(QFLASH_ERR_ARG, "null pointer");
+  qfb::WindowBiasSpec wb;
+  wb.table = table;
+  wb.table_dtype = table_dtype;
+  wb.table_strides[0] = table_strides[0];
+  wb.table_strides[1] = table_strides[1];
+  wb.table_rows = table_rows;
+  wb.index = index;
+  wb.mask = window_mask;
+  wb.mask_dtype = window_mask_dtype;
+  wb.num_windows = num_windows;
+  return qfb::fused_fwd(q, k, v, dtype, q_strides, k_strides, v_strides, nullptr, -1, nullptr, 0, 0, 0, q8, k8, v8,
+                        nullptr, out, out_strides, Z, H, N, D, scale_log2e, l_shift, acc_shift, flags, workspace,
+                        workspace_bytes, stream, &wb);
 }
 
 extern "C" int qflash_fused_status(const void* workspace, void* stream, int64_t* status) {

@@ -38,7 +38,9 @@ ACC_USE_SHIFT = os.environ.get("QFLASH_ACC_USE_SHIFT", "1") == "1"
 L_SHIFT = int(os.environ.get("QFLASH_L_SHIFT", "30"))
 ACC_SHIFT = int(os.environ.get("QFLASH_ACC_SHIFT", "30"))
 DIV_MODE = os.environ.get("QFLASH_DIV", "ieee")
-FUSED = os.environ.get("QFLASH_FUSED", "0") == "1"
+# qflash.forward runs every step on the device (forward_fused) unless
+# QFLASH_FUSED=0 selects the torch-op host path (the reference's own sequence)
+FUSED = os.environ.get("QFLASH_FUSED", "1") == "1"
 
 LOG2E = 1.44269504
 NEG_INF = -(1 << 20)
@@ -175,10 +177,38 @@ def qflash_forward(
     return_mode: str = 'output',
 ):
     """Integer-only attention; same signature, arithmetic and output dtype as
-    the reference's ``qflash.forward`` (qflash/kernel.py:275-351)."""
-    if FUSED and return_mode == 'output':
-        return forward_fused(query, key, value, attn_mask, scale)
+    the reference's ``qflash.forward`` (qflash/kernel.py:275-351).
+
+    By default the whole forward runs on the device (``forward_fused``, bit for
+    bit the same output) with one synchronisation at the end that raises where
+    the reference raises (ZeroDivisionError for an all-zero q or k; ValueError
+    when the constants are not representable).  Inputs it does not take (other
+    dtypes, q/k/v of different shapes, masks that do not broadcast per batch
+    and head) and ``return_mode='latency'`` use the torch-op host path."""
+    if FUSED and return_mode == 'output' and _fused_takes(query, key, value, attn_mask):
+        return forward_fused(query, key, value, attn_mask, scale, check=True)
     return forward_with_scales(query, key, value, attn_mask, scale, return_mode)
+
+
+def _fused_takes(query, key, value, attn_mask) -> bool:
+    if not (query.is_cuda and key.is_cuda and value.is_cuda):
+        return False
+    if query.dtype not in (torch.float32, torch.float16, torch.bfloat16) or not (
+            query.dtype == key.dtype == value.dtype):
+        return False
+    if query.dim() != 4 or not (query.shape == key.shape == value.shape) or query.shape[-1] not in (32, 64, 128, 256):
+        return False
+    if attn_mask is not None:
+        if not attn_mask.is_cuda or attn_mask.dtype not in (torch.float32, torch.float16, torch.bfloat16, torch.bool):
+            return False
+        m = attn_mask
+        while m.dim() < 4:
+            m = m.unsqueeze(0)
+        Z, H, N, _ = query.shape
+        if m.dim() != 4 or m.shape[0] not in (1, Z) or m.shape[1] not in (1, H) or m.shape[2] not in (1, N) \
+                or m.shape[3] not in (1, N):
+            return False
+    return True
 
 
 def forward_fused(query, key, value, attn_mask=None, scale=None, bias_z_period=0, check=False,
@@ -312,6 +342,54 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
     return o * o_scale
 
 
+def forward_window_fused(query, key, value, table, index, window_mask=None, scale=None, check=True, out=None):
+    """QWindowAttention's attention (qflash/attention.py:64-76) with every step
+    on the device, the bias included (qflash_fwd_fused_window): the float mask
+    entry (b, h, i, j) is table[index[i, j], h] + window_mask[b % nW, i, j],
+    formed and quantised once per window and head.  Same bits as
+    ``qflash.forward(q, k, v, attn_mask=<the reference's expanded mask>)``.
+
+    table: [(2wh-1)(2ww-1), H]; index: [N, N] int64; window_mask: [nW, N, N] or
+    None; q/k/v: [B_, H, N, D] with B_ a multiple of nW."""
+    Z, H, N, D = query.shape
+    if not (query.shape == key.shape == value.shape) or D not in (32, 64, 128, 256):
+        raise ValueError("q, k, v must share one [B_, H, N, D] shape with D in {32, 64, 128, 256}")
+    if query.dtype not in (torch.float32, torch.float16, torch.bfloat16) or not (
+            query.dtype == key.dtype == value.dtype):
+        raise ValueError(f"float32/float16/bfloat16 inputs of one dtype, got {query.dtype}")
+    if table.dim() != 2 or table.shape[1] != H or index.numel() != N * N:
+        raise ValueError(f"table must be [T, {H}] and index [{N}, {N}]")
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (query, key, value))
+    dev = q.device
+    idx = index.to(device=dev, dtype=torch.int64).contiguous().view(-1)
+    tab = table.to(dev)
+    nW = 0
+    wm = None
+    if window_mask is not None:
+        wm = window_mask.to(dev).contiguous()
+        nW = wm.shape[0]
+        if wm.shape != (nW, N, N) or Z % nW:
+            raise ValueError(f"window_mask must be [nW, {N}, {N}] with nW dividing {Z}")
+    q8, k8, v8 = (torch.empty((Z, H, N, D), dtype=torch.int8, device=dev) for _ in range(3))
+    if out is None:
+        out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
+    ws = torch.empty(_lib.fused_workspace_bytes(nW if wm is not None else 1, H, N), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.fwd_fused_window(q, k, v, tab, idx, wm, nW, q8, k8, v8, out, scale * LOG2E, L_SHIFT, ACC_SHIFT,
+                          arith_flags(), ws, stream)
+    if check:
+        st = _lib.fused_status(ws, stream)
+        if st == 1:
+            raise ZeroDivisionError("float division by zero (q or k is all zero)")
+        if st == 3:
+            raise IndexError("relative position index outside the bias table")
+        if st != 0:
+            raise ValueError("the fixed-point constants are not representable for this input")
+    return out
+
+
 def window_attention(query, key, value, rel_bias, window_mask=None, scale=None, return_mode='output'):
     """Swin window attention with the bias kept at window granularity.
 
@@ -327,11 +405,14 @@ def window_attention(query, key, value, rel_bias, window_mask=None, scale=None, 
     [1, H, N, N]; window_mask: [nW, N, N] (0 / -100 shifted-window mask) or None.
     """
     if window_mask is None:
-        return forward_with_scales(query, key, value, rel_bias, scale, return_mode)
+        return qflash_forward(query, key, value, rel_bias, scale, return_mode)
     nW, N = window_mask.shape[0], window_mask.shape[-1]
     if query.shape[0] % nW:
         raise ValueError(f"batch {query.shape[0]} is not a multiple of the {nW} windows")
     attn_mask = rel_bias + window_mask.view(nW, 1, N, N)
+    if FUSED and return_mode == 'output' and _fused_takes(query, key, value, None) and attn_mask.is_cuda \
+            and attn_mask.dtype in (torch.float32, torch.float16, torch.bfloat16):
+        return forward_fused(query, key, value, attn_mask, scale, bias_z_period=nW, check=True)
     return forward_with_scales(query, key, value, attn_mask, scale, return_mode, bias_z_period=nW)
 
 

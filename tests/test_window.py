@@ -79,3 +79,61 @@ def test_qwindowattention_module_equals_reference_formulation():
     am = mod._get_rel_pos_bias() + mask.view(1, 16, 1, N, N).expand(2, -1, 3, -1, -1).reshape(-1, 3, N, N)
     ref = mod.proj(K.qflash_forward(q, k, v, attn_mask=am).transpose(1, 2).reshape(B_, N, -1))
     assert torch.equal(out, ref)
+
+
+def _swin_gpu_parts(heads, windows, images, dtype, table_dtype, mask_dtype, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    N, D = 49, 32
+    q, k, v = (torch.randn(images * windows, heads, N, D, generator=g, device="cuda").to(dtype) for _ in range(3))
+    table = (torch.randn(169, heads, generator=g, device="cuda") * 2).to(table_dtype)
+    index = relative_position_index(7, 7).cuda()
+    side = int(windows ** 0.5) * 7
+    mask = shifted_window_mask(side, side, 7, 3).cuda().to(mask_dtype) if windows > 1 else None
+    return q, k, v, table, index, mask
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,table_dtype,mask_dtype", [
+    (torch.float32, torch.float32, torch.float32),
+    (torch.float16, torch.float16, torch.float16),
+    (torch.bfloat16, torch.bfloat16, torch.bfloat16),
+    (torch.float16, torch.float32, torch.float16),    # promoted add in fp32
+    (torch.bfloat16, torch.float16, torch.bfloat16),  # fp16 + bf16 -> fp32
+])
+@pytest.mark.parametrize("windows", [1, 16])
+def test_window_bias_built_on_device_equals_reference_mask(dtype, table_dtype, mask_dtype, windows):
+    """qflash_fwd_fused_window (bias from table, index and mask on the device)
+    equals qflash.forward on the dense [B_, H, N, N] mask QWindowAttention
+    builds (qflash/attention.py:68-72), bit for bit."""
+    heads, images = 3, 2
+    q, k, v, table, index, mask = _swin_gpu_parts(heads, windows, images, dtype, table_dtype, mask_dtype)
+    full = window_attn_mask(table, index, images * windows // (mask.shape[0] if mask is not None else 1)
+                            if mask is not None else images, mask)
+    expect = K.forward_with_scales(q, k, v, full)
+    got = K.forward_window_fused(q, k, v, table, index, mask)
+    assert torch.equal(got, expect)
+
+
+@pytest.mark.gpu
+def test_window_bias_bad_index_raises():
+    q, k, v, table, index, mask = _swin_gpu_parts(3, 16, 1, torch.float16, torch.float16, torch.float16)
+    bad = index.clone()
+    bad[3, 5] = 169
+    with pytest.raises(IndexError):
+        K.forward_window_fused(q, k, v, table, bad, mask)
+    assert torch.isnan(K.forward_window_fused(q, k, v, table, bad, mask, check=False)).all()
+
+
+@pytest.mark.gpu
+def test_qwindowattention_fused_equals_host_path(monkeypatch):
+    from qflash_b200.attention import QWindowAttention
+    torch.manual_seed(0)
+    m = QWindowAttention(96, 3, 7).cuda().half()
+    x = torch.randn(2 * 16, 49, 96, device="cuda", dtype=torch.half)
+    mask = shifted_window_mask(28, 28, 7, 3).cuda().half()
+    monkeypatch.setattr(K, "FUSED", False)
+    ref = m(x, mask)
+    ref_nomask = m(x)
+    monkeypatch.setattr(K, "FUSED", True)
+    assert torch.equal(m(x, mask), ref)
+    assert torch.equal(m(x), ref_nomask)
