@@ -22,6 +22,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 #include <cstring>
 
 #include "../../include/qflash_b200.h"
@@ -62,6 +63,7 @@ __device__ __forceinline__ float rt(float x) {
 struct Rows {
   const void* p;
   long long s0, s1, s2;  // element strides of Z, H, N (the head dim is contiguous)
+  int dense;             // rows packed one after another: element offset = row * D
 };
 
 // max with NaN propagation (torch.amax returns NaN if any element is NaN)
@@ -115,6 +117,7 @@ __device__ __forceinline__ float vec_elem(const uint4& u, int e) {
 
 // element offset of vector i of a [Z, H, N, D] strided tensor (vpr = 1 << vshift vectors per row)
 __device__ __forceinline__ long long vec_offset(const Rows& r, unsigned i, int vshift, int H, int N, int ve) {
+  if (r.dense) return (long long)i * ve;
   const unsigned row = i >> vshift, cv = i & ((1u << vshift) - 1);
   const unsigned c = row % (unsigned)N, t = row / (unsigned)N, b = t % (unsigned)H, a = t / (unsigned)H;
   return (long long)a * r.s0 + (long long)b * r.s1 + (long long)c * r.s2 + (long long)cv * ve;
@@ -136,10 +139,28 @@ __global__ void amax3v_kernel(Rows q, Rows k, Rows v, int H, int N, int vshift, 
       const unsigned i = i0 + j * stride;
       u[j] = i < nvec ? __ldg((const uint4*)(x + vec_offset(r, i, vshift, H, N, VE))) : make_uint4(0, 0, 0, 0);
     }
+    if constexpr (T == kF32) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int e = 0; e < VE; ++e) m = nmax(m, fabsf(vec_elem<T>(u[j], e)));
+        for (int e = 0; e < VE; ++e) m = nmax(m, fabsf(vec_elem<T>(u[j], e)));
+    } else {
+      // |x| max on packed pairs in the input type (exact; NaN propagates like torch.amax)
+      using P2 = typename std::conditional<T == kF16, __half2, __nv_bfloat162>::type;
+      P2 mm2 = *(const P2*)&u[0].x;
+      mm2 = __habs2(mm2);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t w[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) mm2 = __hmax2_nan(mm2, __habs2(*(const P2*)&w[c]));
+      }
+      if constexpr (T == kF16) {
+        m = nmax(m, nmax(__low2float(mm2), __high2float(mm2)));
+      } else {
+        m = nmax(m, nmax(__low2float(mm2), __high2float(mm2)));
+      }
+    }
   }
   for (int o = 16; o; o >>= 1) m = nmax(m, __shfl_xor_sync(0xffffffffu, m, o));
   __shared__ float sm[32];
@@ -459,9 +480,12 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
   const long long nrows_ll = (long long)Z * H * N;
   if (nrows_ll > 0x7fffffffLL) return set_err(QFLASH_ERR_ARG, "too many rows");
   const int nrows = (int)nrows_ll;
-  const Rows rq{q, q_strides[0], q_strides[1], q_strides[2]};
-  const Rows rk{k, k_strides[0], k_strides[1], k_strides[2]};
-  const Rows rv{v, v_strides[0], v_strides[1], v_strides[2]};
+  auto dense = [&](const int64_t* st) {
+    return st[2] == D && st[1] == (int64_t)N * D && st[0] == (int64_t)H * N * D;
+  };
+  const Rows rq{q, q_strides[0], q_strides[1], q_strides[2], dense(q_strides)};
+  const Rows rk{k, k_strides[0], k_strides[1], k_strides[2], dense(k_strides)};
+  const Rows rv{v, v_strides[0], v_strides[1], v_strides[2], dense(v_strides)};
   const int threads = 256, wpb = threads / 32;
   int P = (nrows + wpb - 1) / wpb;
   const int cap = 8 * sm_count(dev);
