@@ -6,7 +6,8 @@ One step = one attention call (``qflash_i8_fwd``) over the whole workload, the
 headline being the ViT-B/16 attention layer (B=256, H=12, N=197, d=64).
 ``value`` is int8 TOPS (4*Z*H*N^2*d ops per call) with the int8 inputs
 resident in HBM; ``e2e`` is the same metric with the int8 Q/K/V copied from
-pinned host memory and O copied back inside the timed region.  With N > 1 GPUs
+pinned host memory and O copied back inside the timed region (steps pipelined
+over copy-in, compute and copy-out streams).  With N > 1 GPUs
 (launched by torchrun) every rank runs the full per-GPU workload on its own
 GPU (weak scaling, no data-path collective) and the time is the max over ranks.
 
@@ -233,27 +234,55 @@ def main():
     ms_step = ms_total / a.steps
     assert _lib.device_error(sp) == 0
 
-    # end to end through the C ABI: pinned host int8 in, int8 out, copies timed
+    # End to end through the C ABI: every step copies its int8 Q/K/V from pinned
+    # host memory and reads its int8 O back, all inside the timed region.  The
+    # steps are pipelined the way a server would run them: copy-in, attention
+    # and copy-out on three streams over two device buffer sets, so step i's
+    # host->device copy overlaps step i-1's kernel and device->host copy (PCIe
+    # is full duplex).
     hq, hk, hv = (t.cpu().pin_memory() for t in (q8, k8, v8))
-    ho = torch.empty(v8.shape, dtype=torch.int8).pin_memory()
-    dq, dk, dv, do = (torch.empty_like(q8) for _ in range(4))
+    ho = [torch.empty(v8.shape, dtype=torch.int8).pin_memory() for _ in range(2)]
+    dbuf = [[torch.empty_like(q8) for _ in range(4)] for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_cmp = torch.cuda.Stream(dev)
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    cmp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+    for ev in cmp_done + out_done:
+        ev.record(stream)
 
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        K.launch_int8(dq, dk, dv, do, rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period)
-        ho.copy_(do, non_blocking=True)
+    def e2e_step(i):
+        b = i & 1
+        dq, dk, dv, do = dbuf[b]
+        s_in.wait_event(cmp_done[b])            # the kernel that read buffer b is done
+        with torch.cuda.stream(s_in):
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            in_done[b].record(s_in)
+        s_cmp.wait_event(in_done[b])
+        s_cmp.wait_event(out_done[b])           # the copy that read output b is done
+        K.launch_int8(dq, dk, dv, do, rs, eM, rM, lM, aM, bias, bstr, stream=s_cmp.cuda_stream,
+                      bias_z_period=period)
+        cmp_done[b].record(s_cmp)
+        s_out.wait_event(cmp_done[b])
+        with torch.cuda.stream(s_out):
+            ho[b].copy_(do, non_blocking=True)
+            out_done[b].record(s_out)
 
-    for _ in range(3):
-        e2e_step()
+    for i in range(3):
+        e2e_step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(a.e2e_steps):
-        e2e_step()
+    for st_ in (s_in, s_cmp, s_out):
+        st_.wait_event(e0)
+    for i in range(a.e2e_steps):
+        e2e_step(i)
+    for ev in out_done:
+        stream.wait_event(ev)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / max(1, a.e2e_steps)
@@ -327,7 +356,8 @@ def main():
                      "tc_frac": round(value / world / 4500.0, 4), "tc_peak_note": "4.5 POPS dense int8 (nominal)"},
         "e2e": {"value": round(ops_rank * world / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": int(3 * w.Z * w.H * w.N * w.D), "d2h_bytes_per_step": int(w.Z * w.H * w.N * w.D),
-                "path": "qflash_i8_fwd via ctypes, pinned host int8 buffers"},
+                "path": "qflash_i8_fwd via ctypes, pinned host int8 buffers, copy-in / kernel / copy-out "
+                        "pipelined on three streams"},
         "cpu_baseline": cpu,
         "gpu_launches": int(launches),
         "clocks": clocks,
