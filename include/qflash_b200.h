@@ -178,6 +178,13 @@ int qflash_fwd_fused_noalloc(const void* q, const void* k, const void* v, int dt
  * wait gives up (0 = none).  Synchronises the stream. */
 int qflash_device_error(void* stream, uint32_t* out);
 
+/* Self-test of the timeout path: one thread waits, with the attention kernel's
+ * bounded wait, on an mbarrier that nothing arrives at; after max_cycles SM
+ * clocks (at most 4e9) it gives up and sets bit 31 of the device error word
+ * (read it with qflash_device_error).  Asynchronous on `stream`, on the
+ * current device.  No counterpart in the reference. */
+int qflash_selftest_wait_timeout(void* stream, long long max_cycles);
+
 /* Number of kernel launches issued by this library since load (for accounting). */
 uint64_t qflash_launch_count(void);
 

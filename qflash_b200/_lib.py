@@ -67,6 +67,7 @@ SIGNATURES = {
     "qflash_last_grid": (ctypes.c_int, []),
     "qflash_version": (ctypes.c_char_p, []),
     "qflash_last_error": (ctypes.c_char_p, []),
+    "qflash_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
 }
 
 _lock = threading.Lock()

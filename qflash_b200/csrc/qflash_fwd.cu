@@ -50,7 +50,7 @@ __device__ unsigned int g_err;       // set when a bounded wait gives up
 
 // Error codes written to g_err (bit set per site).
 enum : unsigned { kErrQEmpty = 1, kErrKvEmpty = 2, kErrQFull = 4, kErrKvFull = 8, kErrPFull = 16,
-                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128 };
+                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128, kErrSelftest = 1u << 31 };
 
 struct KArgs {
   int Z, H, N, nch, ntiles, nitems, ZH;
@@ -1062,6 +1062,35 @@ extern "C" int qflash_device_error(void* stream, uint32_t* out) {
       cudaMemcpyToSymbol(g_err, &zero, sizeof(zero)) != cudaSuccess)
     return set_err(QFLASH_ERR_LAUNCH, "error word: %s", cudaGetErrorString(cudaGetLastError()));
   *out = v;
+  return QFLASH_OK;
+}
+
+namespace qfb {
+// The bounded wait of the attention kernel on an mbarrier that nothing ever
+// arrives at: gives up after max_cycles SM clocks and records kErrSelftest in
+// the error word, as a real timeout would record its site.
+__global__ void wait_selftest_kernel(long long max_cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_u32(&bar);
+  mbar_init(b, 1);
+  fence_mbar_init();
+  const long long t0 = clock64();
+  while (!mbar_try_wait_hint(b, 0, 1000)) {
+    if (clock64() - t0 > max_cycles) {
+      atomicOr(&g_err, kErrSelftest);
+      return;
+    }
+  }
+}
+}  // namespace qfb
+
+extern "C" int qflash_selftest_wait_timeout(void* stream, long long max_cycles) {
+  if (max_cycles < 0 || max_cycles > 4000000000LL) return set_err(QFLASH_ERR_ARG, "max_cycles out of range");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_err(QFLASH_ERR_DEVICE, "no device");
+  qfb::wait_selftest_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(max_cycles);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "selftest launch: %s", cudaGetErrorString(e));
   return QFLASH_OK;
 }
 

@@ -76,3 +76,19 @@ def test_div_full_matches_compiled_reference_on_b200(golden, name):
     o = _run_kernel(rec, flags=K.arith_flags(bool(e), bool(l), bool(a), "full"))
     mism = int((o != gpu["o8"]).sum())
     assert mism == 0, f"{mism} of {o.size} int8 outputs differ from the compiled reference"
+
+
+def test_bounded_wait_reports_timeout_and_context_stays_usable():
+    """A wait on an mbarrier that nothing arrives at gives up after its cycle
+    limit and records the error bit instead of hanging; the context then runs
+    the attention kernel normally."""
+    from qflash_b200 import _lib
+    from qflash_b200 import kernel as K
+    stream = torch.cuda.current_stream().cuda_stream
+    assert _lib.device_error(stream) == 0
+    assert _lib.load().qflash_selftest_wait_timeout(stream, 2_000_000) == 0   # ~1 ms at 1.9 GHz
+    assert _lib.device_error(stream) == 1 << 31
+    assert _lib.device_error(stream) == 0                                     # read-and-clear
+    q, k, v = (torch.randn(1, 2, 64, 64, device="cuda") for _ in range(3))
+    assert torch.equal(K.forward_fused(q, k, v), K.forward_with_scales(q, k, v))
+    assert _lib.device_error(stream) == 0
