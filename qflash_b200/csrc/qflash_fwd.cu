@@ -8,16 +8,17 @@
 // O = int8(int32(fp32(acc) / fp32(l))).
 //
 // Structure of one CTA (192 threads) -- a persistent loop over work items, an
-// item being one 128-query-row tile of one (z, h) head:
+// item being one 128-query-row tile of one (z, h) head, or two heads of <= 64
+// rows packed in one tile:
 //   warps 0-3  softmax: warp w owns TMEM lanes [32w, 32w+32) = query rows of
-//              the tile; acc lives in registers (one row per thread)
+//              the tile; acc lives in TMEM (one row per lane, DV columns)
 //   warp 4     TMA producer: Q tile, then K/V chunk stages (and bias chunks)
 //   warp 5     TMEM allocator and tcgen05.mma issuer
 // Per 32-key chunk g (counted over the CTA's whole item sequence):
 //   MMA   S_g = Q K_g^T            -> TMEM S slot (g & 1), 32 columns
-//   soft  read S_g, exp2/requant, write packed int8 P_g into the same slot
-//   MMA   PV_g = P_g (TMEM) V_g    -> TMEM PV slot (g & 1), DV columns
-//   soft  acc = rescale(acc, alpha_g) + PV_g
+//   soft  read S_g, exp2/requant, write packed int8 P_g into the same slot;
+//         acc = rescale(acc, alpha_g) in place once PV_{g-1} has landed
+//   MMA   acc += P_g (TMEM) V_g
 // The MMA warp issues S_{g+1} before PV_g, so the tensor core computes the
 // next scores while the softmax warps work on the current chunk.
 #include <cuda.h>
