@@ -124,7 +124,7 @@ __device__ __forceinline__ long long vec_offset(const Rows& r, unsigned i, int v
 }
 
 template <int T>
-__global__ void amax3v_kernel(Rows q, Rows k, Rows v, int H, int N, int vshift, unsigned nvec, float* partials) {
+__global__ void __launch_bounds__(256, 8) amax3v_kernel(Rows q, Rows k, Rows v, int H, int N, int vshift, unsigned nvec, float* partials) {
   using E = Elt<T>;
   constexpr int VE = kVecElems<T>;
   const Rows r = blockIdx.y == 0 ? q : (blockIdx.y == 1 ? k : v);
@@ -174,8 +174,9 @@ __global__ void amax3v_kernel(Rows q, Rows k, Rows v, int H, int N, int vshift, 
 }
 
 template <int T>
-__global__ void quantize3v_kernel(Rows q, Rows k, Rows v, int H, int N, int D, int vshift, unsigned nvec,
-                                  const long long* dp, int8_t* q8, int8_t* k8, int8_t* v8) {
+__global__ void __launch_bounds__(256, 8)
+    quantize3v_kernel(Rows q, Rows k, Rows v, int H, int N, int D, int vshift, unsigned nvec, const long long* dp,
+                      int8_t* q8, int8_t* k8, int8_t* v8) {
   using E = Elt<T>;
   constexpr int VE = kVecElems<T>;
   if (dp[P_STATUS] != 0) return;
@@ -191,9 +192,42 @@ __global__ void quantize3v_kernel(Rows q, Rows k, Rows v, int H, int N, int D, i
   // about 127.  Otherwise the IEEE division.
   const bool fastdiv = T != kF32 && s >= 1.2621774e-29f && s <= 7.9228163e+28f;
   const float R = __frcp_rn(s);
-  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += gridDim.x * blockDim.x) {
-    const uint4 u = __ldg((const uint4*)(x + vec_offset(r, i, vshift, H, N, VE)));
+  // one 16-byte vector of x: q = int8(clamp(round(x / s))), packed into the int8 output
+  auto convert = [&](const uint4& u, unsigned i) {
     uint32_t packed[2] = {0u, 0u};
+    if constexpr (T != kF32) {
+      if (fastdiv) {
+        // Here s is finite and |x| <= amax (a NaN or infinite x makes s NaN or
+        // infinite), so q is finite: no NaN case.  Per pair of elements: q in
+        // fp32, one rounding to T, clamp, then round half to even by adding
+        // 1.5 * 2^10 in fp16 (its ulp is 1 on [1024, 2048)) or 1.5 * 2^23 in
+        // fp32 for bf16; the int8 value is the low byte of that sum's bits.
+        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+        uint32_t b[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          float2 f;
+          if constexpr (T == kF16) f = __half22float2(*(const __half2*)&wd[p]);
+          else f = __bfloat1622float2(*(const __nv_bfloat162*)&wd[p]);
+          const float q0a = __fmul_rn(f.x, R), q0b = __fmul_rn(f.y, R);
+          const float qa = __fmaf_rn(__fmaf_rn(-q0a, s, f.x), R, q0a);
+          const float qb = __fmaf_rn(__fmaf_rn(-q0b, s, f.y), R, q0b);
+          if constexpr (T == kF16) {
+            __half2 y = __floats2half2_rn(qa, qb);
+            y = __hadd2(__hmin2(__hmax2(y, __float2half2_rn(-128.f)), __float2half2_rn(127.f)),
+                        __float2half2_rn(1536.f));
+            b[p] = *(const uint32_t*)&y;  // int8 values in bytes 0 and 2
+          } else {
+            const float2 y = __bfloat1622float2(__floats2bfloat162_rn(qa, qb));
+            const float ca = __fadd_rn(fminf(fmaxf(y.x, -128.f), 127.f), 12582912.f);
+            const float cb = __fadd_rn(fminf(fmaxf(y.y, -128.f), 127.f), 12582912.f);
+            b[p] = __byte_perm(__float_as_uint(ca), __float_as_uint(cb), 0x0400);
+          }
+        }
+        *(uint2*)(out + (long long)i * VE) = make_uint2(__byte_perm(b[0], b[1], 0x6420), __byte_perm(b[2], b[3], 0x6420));
+        return;
+      }
+    }
 #pragma unroll
     for (int e = 0; e < VE; ++e) {
       const float xe = vec_elem<T>(u, e);
@@ -215,8 +249,21 @@ __global__ void quantize3v_kernel(Rows q, Rows k, Rows v, int H, int N, int D, i
     int8_t* o = out + (long long)i * VE;
     if constexpr (VE == 8) *(uint2*)o = make_uint2(packed[0], packed[1]);
     else *(uint32_t*)o = packed[0];
-    (void)D;
+  };
+  // four vectors in flight per thread: loads first, then convert and store
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < nvec; i0 += 4 * stride) {
+    uint4 uv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const unsigned i = i0 + j * stride;
+      uv[j] = i < nvec ? __ldg((const uint4*)(x + vec_offset(r, i, vshift, H, N, VE))) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (i0 + j * stride < nvec) convert(uv[j], i0 + j * stride);
   }
+  (void)D;
 }
 
 __device__ __forceinline__ bool fits_i32(double x) { return x >= -2147483648.0 && x <= 2147483647.0; }
@@ -503,10 +550,14 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
     const unsigned nvec = (unsigned)nvec_ll;
     int vshift = 0;
     while ((1 << vshift) < D * esz / 16) ++vshift;
-    int PV = (int)((nvec + 255) / 256);
-    const int capv = 4 * sm_count(dev);
+    // one resident wave over the three tensors (8 blocks of 256 threads per
+    // SM: both kernels use at most 32 registers); a grid of more blocks than
+    // fit runs a partly empty last wave
+    int PV = (int)((nvec + 1023) / 1024);
+    const int capv = 8 * sm_count(dev) / 3;
     PV = PV < capv ? PV : capv;
     PV = PV < kMaxPartials ? PV : kMaxPartials;
+    PV = PV < 1 ? 1 : PV;
     const dim3 gv(PV, 3);
     switch (dtype) {
       case kF32:

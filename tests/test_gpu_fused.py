@@ -139,9 +139,10 @@ def test_quantise_every_16bit_value(dtype):
     bits = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(dtype)
     allv = bits[torch.isfinite(bits.float())].cuda()
     g = torch.Generator(device="cuda").manual_seed(1)
-    # maxima whose scale amax / 127 is a normal number in both dtypes (smaller
-    # ones give s = 0 in fp16: the ZeroDivisionError case)
-    for amax in (0.01, 0.37, 0.7, 1.0, 5.5, 127.0, 3.1e3, 6.0e4):
+    # maxima whose scale amax / 127 is non-zero in both dtypes (below about
+    # 3.8e-6 it is 0 in fp16: the ZeroDivisionError case); 5e-4 and 2e-3 give
+    # subnormal fp16 scales, where |x / s| can pass 127.5 and the clamp acts
+    for amax in (5e-4, 2e-3, 0.01, 0.37, 0.7, 1.0, 5.5, 127.0, 3.1e3, 6.0e4):
         a = torch.tensor(amax, dtype=dtype, device="cuda")
         x = allv[allv.abs() <= a]
         x = torch.cat([x, a.view(1)])
