@@ -142,7 +142,11 @@ def test_quantise_every_16bit_value(dtype):
     # maxima whose scale amax / 127 is non-zero in both dtypes (below about
     # 3.8e-6 it is 0 in fp16: the ZeroDivisionError case); 5e-4 and 2e-3 give
     # subnormal fp16 scales, where |x / s| can pass 127.5 and the clamp acts
-    for amax in (5e-4, 2e-3, 0.01, 0.37, 0.7, 1.0, 5.5, 127.0, 3.1e3, 6.0e4):
+    maxima = [5e-4, 2e-3, 0.01, 0.37, 0.7, 1.0, 5.5, 127.0, 3.1e3, 6.0e4]
+    if dtype == torch.bfloat16:
+        # scales outside [2^-96, 2^96] take the IEEE division path
+        maxima += [1e-30, 1e35]
+    for amax in maxima:
         a = torch.tensor(amax, dtype=dtype, device="cuda")
         x = allv[allv.abs() <= a]
         x = torch.cat([x, a.view(1)])
