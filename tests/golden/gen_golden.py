@@ -6,8 +6,8 @@ the float inputs, the host-derived fixed-point parameters, the int8 tensors and
 int32 bias the kernel was launched with, the int8 output it wrote and the
 dequantised result ``qflash.forward`` returned.
 
-Only this script reads the reference (path given by --ref, default the
-read-only mount this build was made against).  It must run where the reference
+Only this script reads the reference (its checkout root given by --ref or
+the QFLASH_REFERENCE_ROOT environment variable).  It must run where the reference
 and Triton are available; the .npz files it writes are committed and are all
 the tests need.
 
@@ -206,7 +206,9 @@ def cases():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("QFLASH_REFERENCE_ROOT"),
+                    required="QFLASH_REFERENCE_ROOT" not in os.environ,
+                    help="root of the reference checkout (or set QFLASH_REFERENCE_ROOT)")
     ap.add_argument("--only", default=None)
     a = ap.parse_args()
     mods = {}
