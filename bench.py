@@ -291,6 +291,32 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    # The scaling runs' result collective, timed apart from the kernel: an NCCL
+    # all_gather of every rank's int8 O shard (what forward_sharded(gather=True)
+    # does); CUDA events on the current stream, max over ranks.
+    gather = None
+    if world > 1:
+        o_loc = sets[0][3]
+        parts = [torch.empty_like(o_loc) for _ in range(world)]
+        for _ in range(2):
+            dist.all_gather(parts, o_loc)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_g = 10
+        g0.record(stream)
+        for _ in range(n_g):
+            dist.all_gather(parts, o_loc)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([g0.elapsed_time(g1) / n_g], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        g_ms = float(t.item())
+        nb = o_loc.numel() * o_loc.element_size()
+        gather = {"collective": "all_gather of the int8 O shards (NCCL)", "bytes_per_rank": int(nb),
+                  "ms": round(g_ms, 4), "busbw_gbs": round(nb * (world - 1) / (g_ms * 1e-3) / 1e9, 1)}
+        del parts
+
     # parity spot check and CPU baseline on a bounded sample of heads (rank 0, N=1 only)
     cpu = None
     sample_exact = None
@@ -359,6 +385,7 @@ def main():
                 "path": "qflash_i8_fwd via ctypes, pinned host int8 buffers, copy-in / kernel / copy-out "
                         "pipelined on three streams"},
         "cpu_baseline": cpu,
+        "gather": gather,
         "gpu_launches": int(launches),
         "clocks": clocks,
         "parity_sample_bit_exact": sample_exact,
