@@ -635,10 +635,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
           }
         }
         // P and acc are ready: release the MMA warp before the bookkeeping below,
-        // which only later chunks need.  The P store (and, when the rescale was
-        // skipped, only it) completes before the fence and the arrive that let
-        // the MMA read it.
-        tmem_wait_st();
+        // which only later chunks need
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(slot));
