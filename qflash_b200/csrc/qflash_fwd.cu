@@ -55,6 +55,7 @@ enum : unsigned { kErrQEmpty = 1, kErrKvEmpty = 2, kErrQFull = 4, kErrKvFull = 8
 
 struct KArgs {
   int Z, H, N, nch, ntiles, nitems, ZH;
+  int rpi;                   // query rows per work item (one head per tile): 128, or 64 / 32 for small grids
   int bias_hb, bias_zb;      // 1 if the bias has a real H / Z dimension, 0 if broadcast
   int bias_zmod;             // > 0: the bias batch index is z mod bias_zmod (Swin window period)
   int v_col0;                // first output column handled (head dim 256 runs as two halves)
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     int zh;
     if (SEGS == 1) {
       zh = item / a.ntiles;
-      row0 = (item - zh * a.ntiles) * kBM;
+      row0 = (item - zh * a.ntiles) * a.rpi;
     } else {
       zh = item * SEGS + sg;
       row0 = 0;
@@ -479,7 +480,9 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
       int z, h, rbase;
       const bool seg_ok = decode(item, sg, z, h, rbase);
       const int row0 = rbase + (SEGS == 1 ? warp : warp % (4 / SEGS)) * 32;
-      const bool active = seg_ok && row0 < a.N;
+      // an item of fewer than 128 rows leaves the warps past them idle (their
+      // lanes hold the next item's rows, computed by another CTA)
+      const bool active = seg_ok && row0 < a.N && (SEGS != 1 || warp * 32 < a.rpi);
       const int row = row0 + lane;
       const bool row_ok = row < a.N;
       int m = kNegInf, l = 1;
@@ -837,8 +840,27 @@ static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const C
     ctas = per_sm[dev];
   }
   int grid = sm_count(dev) * ctas;
-  if (grid > ka.nitems) grid = ka.nitems;
-  kern<<<grid, kThreads, C::SMEM, stream>>>(mq, mk, mv, mb, ka);
+  // A grid that would leave CTA slots empty takes smaller work items: 64 or
+  // 32 query rows of a head (the CTA still loads and multiplies a 128-row Q
+  // box; warps past the item's rows idle), as many as one resident wave holds.
+  // QFLASH_ROWS_PER_ITEM (32, 64 or 128) forces the choice.
+  KArgs kb = ka;
+  if (SEGS == 1) {
+    auto items_for = [&](int rpi) { return (long long)ka.ZH * ((ka.N + rpi - 1) / rpi); };
+    int rpi = kBM;
+    if (const char* e = getenv("QFLASH_ROWS_PER_ITEM")) {
+      const int f = atoi(e);
+      if (f == 32 || f == 64 || f == 128) rpi = f;
+    } else {
+      while (rpi > 32 && items_for(rpi / 2) <= grid) rpi /= 2;
+    }
+    if (items_for(rpi) > 0x7fffffffLL) rpi = kBM;
+    kb.rpi = rpi;
+    kb.ntiles = (ka.N + rpi - 1) / rpi;
+    kb.nitems = (int)items_for(rpi);
+  }
+  if (grid > kb.nitems) grid = kb.nitems;
+  kern<<<grid, kThreads, C::SMEM, stream>>>(mq, mk, mv, mb, kb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -911,6 +933,7 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
   ka.nch = (N + kBN - 1) / kBN;
   // two heads per 128-row tile when a head has at most 64 query rows
   const int segs = (N <= kBM / 2 && (D == 32 || D == 64)) ? 2 : 1;
+  ka.rpi = kBM;
   ka.ntiles = segs == 2 ? 1 : (N + kBM - 1) / kBM;
   const long long zh_total = (long long)Z * H;
   if (zh_total > 0x7fffffffLL) return set_err(QFLASH_ERR_ARG, "too many heads");

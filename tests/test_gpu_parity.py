@@ -38,6 +38,20 @@ def test_kernel_matches_reference(golden, name):
     assert mism == 0, f"{mism} of {o.size} int8 outputs differ"
 
 
+@pytest.mark.parametrize("rpi", ["32", "64", "128"])
+@pytest.mark.parametrize("name", ["cfg1_vit_s", "cfg5_vit_l", "n129_d64", "n100_d32", "n65_d32", "n197_d128",
+                                  "n80_d256", "env_exp_idiv", "env_acc_idiv", "env_shift40", "bool_mask",
+                                  "expm_check_1100", "expm_wrap"])
+def test_rows_per_item_forced(golden, name, rpi, monkeypatch):
+    """Work items of 32, 64 and 128 query rows (chosen by grid size unless
+    QFLASH_ROWS_PER_ITEM forces one) give the same bit-exact output."""
+    monkeypatch.setenv("QFLASH_ROWS_PER_ITEM", rpi)
+    rec = golden(name)
+    o = _run_kernel(rec)
+    mism = int((o != rec["o8"]).sum())
+    assert mism == 0, f"{mism} of {o.size} int8 outputs differ"
+
+
 @pytest.mark.parametrize("name", ["cfg1_vit_s", "cfg3_deit_t", "bench_a2_fp16", "n80_d256"])
 def test_forward_end_to_end(golden, name):
     """qflash.forward on the float inputs: same int8 output, same returned values."""
