@@ -206,6 +206,29 @@ __device__ __forceinline__ void store_dequant32(void* dst, const uint32_t (&res)
   }
 }
 
+// The constants could not be formed (where the reference raises): the
+// dequantised output of this pass (columns [v_col0, v_col0 + DV)) is NaN, the
+// input dtype's rounding of an fp32 quiet NaN.  Grid-stride over all rows.
+template <int DV>
+__device__ void fill_out_nan(const KArgs& a) {
+  const float qnan = __int_as_float(0x7fc00000);
+  const long long n = (long long)a.Z * a.H * a.N * DV;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const long long r = i / DV, d = i - r * DV;
+    const long long t = r / a.N, c = r - t * a.N;
+    const long long z = t / a.H, h = t - z * a.H;
+    const long long off = z * a.ou_z + h * a.ou_h + c * a.ou_n + a.v_col0 + d;
+    if (a.out_dtype == kF32) {
+      ((float*)a.out)[off] = qnan;
+    } else if (a.out_dtype == kF16) {
+      ((__half*)a.out)[off] = __float2half_rn(qnan);
+    } else {
+      ((__nv_bfloat16*)a.out)[off] = __float2bfloat16_rn(qnan);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 // SEGS = 2 packs two heads (of N <= 64 rows each) into one 128-row tile:
 // rows [0, 64) belong to head 2*item, rows [64, 128) to head 2*item + 1.
@@ -262,7 +285,10 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
   KArgs a = a_in;
   if (a_in.dparams) {
     const long long* dp = a_in.dparams;
-    if (dp[0] != 0) return;  // the constants could not be formed (reported by the parameter kernel)
+    if (dp[0] != 0) {  // the constants could not be formed (reported by the parameter kernel)
+      if (a_in.out) fill_out_nan<DV>(a_in);
+      return;
+    }
     a.rs = (int)dp[1];
     a.eM = (int)dp[2];
     a.rM = (int)dp[3];
@@ -791,6 +817,34 @@ static int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, ui
   if (((uintptr_t)base & 15) || (s_row & 15) || (s_h & 15) || (s_z & 15))
     return set_err(QFLASH_ERR_ALIGN, "TMA needs 16-byte aligned base and strides (base %p, strides %llu %llu %llu)",
                    base, (unsigned long long)s_row, (unsigned long long)s_h, (unsigned long long)s_z);
+  // The encoding is a function of these arguments alone, so recent ones are
+  // reused: repeated calls on the same buffers (a caching allocator hands the
+  // same addresses back) skip the driver call.
+  struct Key {
+    const void* base;
+    uint64_t v[7];
+    uint32_t box_cols, box_rows;
+    int dt, atom;
+  };
+  Key key;
+  memset(&key, 0, sizeof(Key));  // padding bytes take part in the comparison
+  key.base = base;
+  const uint64_t kv[7] = {cols, rows, H, Z, s_row, s_h, s_z};
+  memcpy(key.v, kv, sizeof(kv));
+  key.box_cols = box_cols;
+  key.box_rows = box_rows;
+  key.dt = (int)dt;
+  key.atom = atom_bytes;
+  constexpr int kSlots = 16;
+  static thread_local Key keys[kSlots];
+  static thread_local CUtensorMap maps[kSlots];
+  static thread_local int used = 0, next = 0;
+  for (int i = 0; i < used; ++i) {
+    if (memcmp(&keys[i], &key, sizeof(Key)) == 0) {
+      *m = maps[i];
+      return QFLASH_OK;
+    }
+  }
   cuuint64_t dims[4] = {cols, rows, H, Z};
   cuuint64_t strides[3] = {s_row, s_h, s_z};
   cuuint32_t box[4] = {box_cols, box_rows, 1, 1};
@@ -798,6 +852,10 @@ static int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, ui
   CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    tma_swizzle(atom_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_err(QFLASH_ERR_TMA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  memcpy(&keys[next], &key, sizeof(Key));
+  maps[next] = *m;
+  next = (next + 1) % kSlots;
+  if (used < kSlots) ++used;
   return QFLASH_OK;
 }
 

@@ -462,19 +462,6 @@ __global__ void window_bias_kernel(WindowBiasSpec wb, int H, int N, int N4, int 
 
 // NaN into every element of a strided output when the constants could not be
 // formed (the attention kernel then wrote nothing); does nothing otherwise
-template <int T>
-__global__ void nan_fill_kernel(void* out, long long s0, long long s1, long long s2, int H, int N, int D, long long n,
-                                const long long* dp) {
-  if (dp[P_STATUS] == 0) return;
-  using E = Elt<T>;
-  typename E::type* y = (typename E::type*)out;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / D, d = i - r * D;
-    const long long t = r / N, c = r - t * N;
-    const long long a = t / H, b = t - a * H;
-    y[a * s0 + b * s1 + c * s2 + d] = E::t(__int_as_float(0x7fc00000));
-  }
-}
 
 int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int64_t q_strides[4],
               const int64_t k_strides[4], const int64_t v_strides[4], const void* mask, int mask_dtype,
@@ -628,25 +615,10 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
     os.p = out;
     os.dtype = dtype;
     for (int i = 0; i < 4; ++i) os.strides[i] = out_strides ? out_strides[i] : st8[i];
-    int rc = attention_fwd(q8, k8, v8, nullptr, has_mask ? bias : nullptr, st8, st8, st8, nullptr,
-                           has_mask ? bstr : nullptr, has_mask ? mask_z_period : 0, Z, H, N, D, 0, 0, 0, 0, 0, l_shift,
-                           acc_shift, flags, dp, &os, stream);
-    if (rc) return rc;
-    const int ngrid = sm_count(dev);
-    switch (dtype) {
-      case kF32:
-        nan_fill_kernel<kF32><<<ngrid, 256, 0, stream>>>(out, os.strides[0], os.strides[1], os.strides[2], H, N, D, n, dp);
-        break;
-      case kF16:
-        nan_fill_kernel<kF16><<<ngrid, 256, 0, stream>>>(out, os.strides[0], os.strides[1], os.strides[2], H, N, D, n, dp);
-        break;
-      default:
-        nan_fill_kernel<kBF16><<<ngrid, 256, 0, stream>>>(out, os.strides[0], os.strides[1], os.strides[2], H, N, D, n, dp);
-        break;
-    }
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "output launch: %s", cudaGetErrorString(e));
-    return QFLASH_OK;
+    // on an error status the attention kernel writes the NaN output itself
+    return attention_fwd(q8, k8, v8, nullptr, has_mask ? bias : nullptr, st8, st8, st8, nullptr,
+                         has_mask ? bstr : nullptr, has_mask ? mask_z_period : 0, Z, H, N, D, 0, 0, 0, 0, 0, l_shift,
+                         acc_shift, flags, dp, &os, stream);
   }
   int rc = attention_fwd(q8, k8, v8, o8, has_mask ? bias : nullptr, st8, st8, st8, st8, has_mask ? bstr : nullptr,
                          has_mask ? mask_z_period : 0, Z, H, N, D, 0, 0, 0, 0, 0, l_shift, acc_shift, flags, dp,
@@ -719,8 +691,21 @@ extern "C" int qflash_fwd_fused_window(const void* q, const void* k, const void*
 
 extern "C" int qflash_fused_status(const void* workspace, void* stream, int64_t* status) {
   if (!workspace || !status) return qfb::set_err(QFLASH_ERR_ARG, "null pointer");
-  cudaError_t e = cudaMemcpyAsync(status, workspace, sizeof(int64_t), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  // read through a pinned word of this thread (a copy into pageable memory is
+  // staged by the driver); plain copy if pinned memory cannot be had
+  static thread_local int64_t* pinned = nullptr;
+  static thread_local bool tried = false;
+  if (!tried) {
+    tried = true;
+    if (cudaHostAlloc((void**)&pinned, sizeof(int64_t), cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      pinned = nullptr;
+    }
+  }
+  int64_t* dst = pinned ? pinned : status;
+  cudaError_t e = cudaMemcpyAsync(dst, workspace, sizeof(int64_t), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
   if (e != cudaSuccess) return qfb::set_err(QFLASH_ERR_LAUNCH, "status read: %s", cudaGetErrorString(e));
+  if (pinned) *status = *pinned;
   return QFLASH_OK;
 }

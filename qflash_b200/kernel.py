@@ -254,7 +254,7 @@ def forward_fused(query, key, value, attn_mask=None, scale=None, bias_z_period=0
         mask = m
         mstr = [0 if m.shape[i] == 1 else m.stride(i) for i in range(4)]
     dev = q.device
-    q8, k8, v8 = (torch.empty((Z, H, N, D), dtype=torch.int8, device=dev) for _ in range(3))
+    q8, k8, v8 = torch.empty((3, Z, H, N, D), dtype=torch.int8, device=dev).unbind(0)  # one allocation
     if out is None:
         out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
     elif out.shape != (Z, H, N, D) or out.dtype != q.dtype or out.stride(-1) != 1 or out.device != dev:
@@ -372,7 +372,7 @@ def forward_window_fused(query, key, value, table, index, window_mask=None, scal
         nW = wm.shape[0]
         if wm.shape != (nW, N, N) or Z % nW:
             raise ValueError(f"window_mask must be [nW, {N}, {N}] with nW dividing {Z}")
-    q8, k8, v8 = (torch.empty((Z, H, N, D), dtype=torch.int8, device=dev) for _ in range(3))
+    q8, k8, v8 = torch.empty((3, Z, H, N, D), dtype=torch.int8, device=dev).unbind(0)  # one allocation
     if out is None:
         out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
     ws = torch.empty(_lib.fused_workspace_bytes(nW if wm is not None else 1, H, N), dtype=torch.uint8, device=dev)
