@@ -173,17 +173,119 @@ __global__ void __launch_bounds__(256, 8) amax3v_kernel(Rows q, Rows k, Rows v, 
   }
 }
 
+__device__ __forceinline__ bool fits_i32(double x) { return x >= -2147483648.0 && x <= 2147483647.0; }
+
+// Scales and fixed-point constants (qflash/kernel.py:290-307); one block
+// reduces the partial maxima, its first thread does the scalar math.
+template <int T>
+__device__ __noinline__ void block_params(const float* partials, int P, double scale_log2e, int l_shift, int acc_shift, int D,
+                             long long* dp) {
+  __shared__ float red[3][32];
+  float m[3] = {0.f, 0.f, 0.f};
+  for (int i = threadIdx.x; i < P; i += blockDim.x)
+    for (int t = 0; t < 3; ++t) m[t] = nmax(m[t], partials[t * P + i]);
+  for (int t = 0; t < 3; ++t) {
+    float v = m[t];
+    for (int o = 16; o; o >>= 1) v = nmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) red[t][threadIdx.x >> 5] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (int t = 0; t < 3; ++t) {
+    m[t] = red[t][0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m[t] = nmax(m[t], red[t][w]);
+  }
+  const float inv127 = (float)(1.0 / 127.0);
+  const float qs = rt<T>(m[0] * inv127), ks = rt<T>(m[1] * inv127), os = rt<T>(m[2] * inv127);
+  const float qk = rt<T>(qs * ks);
+  const double sm = scale_log2e * (double)qk;
+  long long st = 0;
+  long long rs = 0, eM = 0, rM = 0, lM = 0, aM = 0, mlim = 0;
+  if (sm == 0.0) {
+    st = 1;  // 1.0 / sm_scale: ZeroDivisionError in the reference
+  } else if (!(fabs(sm) < INFINITY)) {
+    st = 2;  // NaN / inf: round() raises in the reference
+  } else {
+    const double rsd = rint(1.0 / sm);
+    const double eMd = rint(-sm * 65536.0);
+    const double rMd = rint(sm * 127.0 * 65536.0);
+    if (rsd == 0.0) {
+      st = 1;  // (1 << L_SHIFT) / sm_rscale
+    } else if (!fits_i32(rsd) || !fits_i32(eMd) || !fits_i32(rMd) || rsd < 0.0) {
+      st = 2;  // outside what the int32 kernel arguments hold
+    } else {
+      rs = (long long)rsd;
+      eM = (long long)eMd;
+      rM = (long long)rMd;
+      lM = (long long)rint((double)(1ll << l_shift) / rsd);
+      aM = (long long)rint((double)(1ll << acc_shift) / rsd);
+      // the exp2_fast range bound (see attention_fwd)
+      const long long S0 = ((long long)D << 14) > (1ll << 20) ? ((long long)D << 14) : (1ll << 20);
+      const long long aem = -eM;
+      const long long lim31 = (1ll << 31) - 1;
+      long long X = aem > 0 ? (lim31 - 65536) / aem : lim31;
+      const long long X2 = ((lim31 - 2ll * rs - 2) * 65536) / (aem * rs + 65536);
+      X = X < X2 ? X : X2;
+      mlim = eM > 0 ? -(1ll << 31) : X - S0;
+      if (mlim > lim31) mlim = lim31;
+      if (mlim < -(1ll << 31)) mlim = -(1ll << 31);
+    }
+  }
+  dp[P_STATUS] = st;
+  dp[P_RS] = rs;
+  dp[P_EM] = eM;
+  dp[P_RM] = rM;
+  dp[P_LM] = lM;
+  dp[P_ACCM] = aM;
+  dp[P_MLIM] = mlim;
+  dp[P_SM] = __double_as_longlong(sm);
+  dp[P_QS] = __float_as_int(qs);
+  dp[P_KS] = __float_as_int(ks);
+  dp[P_OS] = __float_as_int(os);
+  dp[P_INVSM] = __float_as_int((float)(1.0 / sm));  // torch forms the reciprocal of a scalar in double
+}
+
+template <int T>
+__global__ void params_kernel(const float* partials, int P, double scale_log2e, int l_shift, int acc_shift, int D,
+                              long long* dp) {
+  block_params<T>(partials, P, scale_log2e, l_shift, acc_shift, D, dp);
+}
+
+// The scale of tensor t as block_params forms it: rt<T>(max of its P partial
+// maxima * fl32(1/127)), reduced by one block.
+template <int T>
+__device__ float block_tensor_scale(const float* partials, int P, int t) {
+  __shared__ float red[32];
+  __shared__ float s_out;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) m = nmax(m, partials[t * P + i]);
+  for (int o = 16; o; o >>= 1) m = nmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mm = nmax(mm, red[w]);
+    s_out = rt<T>(mm * (float)(1.0 / 127.0));
+  }
+  __syncthreads();
+  return s_out;
+}
+
 template <int T>
 __global__ void __launch_bounds__(256, 8)
-    quantize3v_kernel(Rows q, Rows k, Rows v, int H, int N, int D, int vshift, unsigned nvec, const long long* dp,
-                      int8_t* q8, int8_t* k8, int8_t* v8) {
+    quantize3v_kernel(Rows q, Rows k, Rows v, int H, int N, int D, int vshift, unsigned nvec, const float* partials,
+                      int P, double scale_log2e, int l_shift, int acc_shift, long long* dp, int8_t* q8, int8_t* k8,
+                      int8_t* v8) {
   using E = Elt<T>;
   constexpr int VE = kVecElems<T>;
-  if (dp[P_STATUS] != 0) return;
   const int t = blockIdx.y;
   const Rows r = t == 0 ? q : (t == 1 ? k : v);
   int8_t* out = t == 0 ? q8 : (t == 1 ? k8 : v8);
-  const float s = __int_as_float((int)dp[P_QS + t]);
+  // The scale comes from the |max| pass's partial maxima (as block_params forms
+  // it); block (0, 0) also writes the constants at the end, for the kernels
+  // after this one.  When the constants cannot be formed the int8 values are
+  // unused (the output is NaN).
+  const float s = block_tensor_scale<T>(partials, P, t);
   const typename E::type* x = (const typename E::type*)r.p;
   // x / s: for 16-bit inputs with s in [2^-96, 2^96] as RN(x * RN(1/s)) plus one
   // FMA residual step, which equals the IEEE quotient for every 16-bit x with
@@ -263,80 +365,11 @@ __global__ void __launch_bounds__(256, 8)
     for (int j = 0; j < 4; ++j)
       if (i0 + j * stride < nvec) convert(uv[j], i0 + j * stride);
   }
+  if (blockIdx.x == 0 && blockIdx.y == 0) block_params<T>(partials, P, scale_log2e, l_shift, acc_shift, D, dp);
   (void)D;
 }
 
-__device__ __forceinline__ bool fits_i32(double x) { return x >= -2147483648.0 && x <= 2147483647.0; }
 
-// Scales and fixed-point constants (qflash/kernel.py:290-307); one block
-// reduces the partial maxima, its first thread does the scalar math.
-template <int T>
-__global__ void params_kernel(const float* partials, int P, double scale_log2e, int l_shift, int acc_shift, int D,
-                              long long* dp) {
-  __shared__ float red[3][32];
-  float m[3] = {0.f, 0.f, 0.f};
-  for (int i = threadIdx.x; i < P; i += blockDim.x)
-    for (int t = 0; t < 3; ++t) m[t] = nmax(m[t], partials[t * P + i]);
-  for (int t = 0; t < 3; ++t) {
-    float v = m[t];
-    for (int o = 16; o; o >>= 1) v = nmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if ((threadIdx.x & 31) == 0) red[t][threadIdx.x >> 5] = v;
-  }
-  __syncthreads();
-  if (threadIdx.x != 0) return;
-  for (int t = 0; t < 3; ++t) {
-    m[t] = red[t][0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m[t] = nmax(m[t], red[t][w]);
-  }
-  const float inv127 = (float)(1.0 / 127.0);
-  const float qs = rt<T>(m[0] * inv127), ks = rt<T>(m[1] * inv127), os = rt<T>(m[2] * inv127);
-  const float qk = rt<T>(qs * ks);
-  const double sm = scale_log2e * (double)qk;
-  long long st = 0;
-  long long rs = 0, eM = 0, rM = 0, lM = 0, aM = 0, mlim = 0;
-  if (sm == 0.0) {
-    st = 1;  // 1.0 / sm_scale: ZeroDivisionError in the reference
-  } else if (!(fabs(sm) < INFINITY)) {
-    st = 2;  // NaN / inf: round() raises in the reference
-  } else {
-    const double rsd = rint(1.0 / sm);
-    const double eMd = rint(-sm * 65536.0);
-    const double rMd = rint(sm * 127.0 * 65536.0);
-    if (rsd == 0.0) {
-      st = 1;  // (1 << L_SHIFT) / sm_rscale
-    } else if (!fits_i32(rsd) || !fits_i32(eMd) || !fits_i32(rMd) || rsd < 0.0) {
-      st = 2;  // outside what the int32 kernel arguments hold
-    } else {
-      rs = (long long)rsd;
-      eM = (long long)eMd;
-      rM = (long long)rMd;
-      lM = (long long)rint((double)(1ll << l_shift) / rsd);
-      aM = (long long)rint((double)(1ll << acc_shift) / rsd);
-      // the exp2_fast range bound (see attention_fwd)
-      const long long S0 = ((long long)D << 14) > (1ll << 20) ? ((long long)D << 14) : (1ll << 20);
-      const long long aem = -eM;
-      const long long lim31 = (1ll << 31) - 1;
-      long long X = aem > 0 ? (lim31 - 65536) / aem : lim31;
-      const long long X2 = ((lim31 - 2ll * rs - 2) * 65536) / (aem * rs + 65536);
-      X = X < X2 ? X : X2;
-      mlim = eM > 0 ? -(1ll << 31) : X - S0;
-      if (mlim > lim31) mlim = lim31;
-      if (mlim < -(1ll << 31)) mlim = -(1ll << 31);
-    }
-  }
-  dp[P_STATUS] = st;
-  dp[P_RS] = rs;
-  dp[P_EM] = eM;
-  dp[P_RM] = rM;
-  dp[P_LM] = lM;
-  dp[P_ACCM] = aM;
-  dp[P_MLIM] = mlim;
-  dp[P_SM] = __double_as_longlong(sm);
-  dp[P_QS] = __float_as_int(qs);
-  dp[P_KS] = __float_as_int(ks);
-  dp[P_OS] = __float_as_int(os);
-  dp[P_INVSM] = __float_as_int((float)(1.0 / sm));  // torch forms the reciprocal of a scalar in double
-}
 
 // int8(clamp(round(x / scale), -128, 127)) into contiguous [Z, H, N, D]
 template <int T>
@@ -549,18 +582,18 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
     switch (dtype) {
       case kF32:
         amax3v_kernel<kF32><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, vshift, nvec, partials);
-        params_kernel<kF32><<<1, 256, 0, stream>>>(partials, PV, sl, l_shift, acc_shift, D, dp);
-        quantize3v_kernel<kF32><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, dp, q8, k8, v8);
+        quantize3v_kernel<kF32><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, partials, PV, sl, l_shift,
+                                                        acc_shift, dp, q8, k8, v8);
         break;
       case kF16:
         amax3v_kernel<kF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, vshift, nvec, partials);
-        params_kernel<kF16><<<1, 256, 0, stream>>>(partials, PV, sl, l_shift, acc_shift, D, dp);
-        quantize3v_kernel<kF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, dp, q8, k8, v8);
+        quantize3v_kernel<kF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, partials, PV, sl, l_shift,
+                                                        acc_shift, dp, q8, k8, v8);
         break;
       default:
         amax3v_kernel<kBF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, vshift, nvec, partials);
-        params_kernel<kBF16><<<1, 256, 0, stream>>>(partials, PV, sl, l_shift, acc_shift, D, dp);
-        quantize3v_kernel<kBF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, dp, q8, k8, v8);
+        quantize3v_kernel<kBF16><<<gv, 256, 0, stream>>>(rq, rk, rv, H, N, D, vshift, nvec, partials, PV, sl, l_shift,
+                                                        acc_shift, dp, q8, k8, v8);
         break;
     }
   } else switch (dtype) {
