@@ -28,12 +28,16 @@ extern "C" {
 #define QFLASH_ERR_UNSUPPORTED (-6) /* combination not implemented */
 
 /* flags: the reference's QFLASH_* arithmetic switches (qflash/kernel.py:30-36)
- * and the final-division rounding. 0 = the reference defaults. */
+ * and the final-division rounding. 0 = the reference defaults, with the final
+ * division acc / l (kernel.py:176) rounded as the reference's compiled Triton
+ * kernel rounds it on B200: Triton lowers the int32 / int32 division to the
+ * approximate fp32 divide div.full.f32. */
 #define QFLASH_FLAG_EXP_IDIV 1u  /* QFLASH_EXP_USE_SHIFT=0: exp2_i32_idiv (kernel.py:47-51) */
 #define QFLASH_FLAG_L_IDIV 2u    /* QFLASH_L_USE_SHIFT=0: scale_release_idiv for l (kernel.py:72-74) */
 #define QFLASH_FLAG_ACC_IDIV 4u  /* QFLASH_ACC_USE_SHIFT=0: scale_release_idiv for acc */
-#define QFLASH_FLAG_DIV_FULL 8u  /* final acc/l with the approximate fp32 divide (div.full.f32) that the
-                                    reference's compiled GPU kernel uses; default is IEEE round-to-nearest */
+#define QFLASH_FLAG_DIV_FULL 8u  /* final division as div.full.f32 (the default; accepted for explicitness) */
+#define QFLASH_FLAG_DIV_IEEE 16u /* final division IEEE round-to-nearest: the reference's algorithm as its
+                                    interpreted (TRITON_INTERPRET=1, numpy) run computes it */
 
 /*
  * Integer attention forward: O = int8(acc / l) of the chunked integer online

@@ -245,8 +245,23 @@ def quantize_bias_bool(attn_mask: np.ndarray) -> np.ndarray:
     return np.where(np.asarray(attn_mask, dtype=bool), 0, NEG_INF).astype(np.int32)
 
 
+def exact_quotients(q8, k8, v8, p: Params, bias=None, **flags) -> np.ndarray:
+    """Boolean [Z, H, N, D]: where acc / l is an exact nonzero integer.
+
+    These are the only elements where the reference's compiled GPU kernel
+    (whose ``acc / l`` at qflash/kernel.py:176 is the approximate fp32 divide
+    div.full.f32, at most 2 ulp from the quotient) can truncate differently
+    from the IEEE division ``div_to_int8`` restates: while |acc| < 2^21 every
+    other quotient is at least 1/l > 2.5 ulp away from an integer.  There it
+    can land one below the integer, i.e. one step toward zero."""
+    _, acc, l = attention_int8(q8, k8, v8, p, bias, return_state=True, **flags)
+    l = l[..., None].astype(np.int64)
+    acc = acc.astype(np.int64)
+    return (acc != 0) & (l > 0) & (acc % np.maximum(l, 1) == 0)
+
+
 def sqnr_db(ref: np.ndarray, out: np.ndarray) -> float:
-    """benchmark.py:140 -- 20 log10(|ref| / |out - ref|)."""
+    """benchmark.py:28 -- 20 log10(|ref| / |out - ref|)."""
     ref = np.asarray(ref, dtype=np.float64)
     out = np.asarray(out, dtype=np.float64)
     return float(20.0 * math.log10(np.linalg.norm(ref) / np.linalg.norm(out - ref)))

@@ -16,6 +16,7 @@ FLAG_EXP_IDIV = 1
 FLAG_L_IDIV = 2
 FLAG_ACC_IDIV = 4
 FLAG_DIV_FULL = 8
+FLAG_DIV_IEEE = 16
 
 ERRORS = {-1: "QFLASH_ERR_ARG", -2: "QFLASH_ERR_ALIGN", -3: "QFLASH_ERR_TMA", -4: "QFLASH_ERR_LAUNCH",
           -5: "QFLASH_ERR_DEVICE", -6: "QFLASH_ERR_UNSUPPORTED"}

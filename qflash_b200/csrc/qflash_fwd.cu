@@ -51,7 +51,8 @@ __device__ unsigned int g_err;       // set when a bounded wait gives up
 
 // Error codes written to g_err (bit set per site).
 enum : unsigned { kErrQEmpty = 1, kErrKvEmpty = 2, kErrQFull = 4, kErrKvFull = 8, kErrPFull = 16,
-                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128, kErrSelftest = 1u << 31 };
+                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128, kErrV2Ready = 256, kErrV2Src = 512,
+                  kErrSelftest = 1u << 31 };
 
 struct KArgs {
   int Z, H, N, nch, ntiles, nitems, ZH;
@@ -149,40 +150,37 @@ __device__ __forceinline__ int rel_idiv(int x, int alpha, int rs) {
   return (int)((unsigned)x * (unsigned)alpha) / rs;
 }
 
-// Final division (qflash/kernel.py:176): int32(fp32(acc) / fp32(l)); a NaN or
-// out-of-range quotient becomes INT32_MIN.
-__device__ __forceinline__ int div_to_i32(int acc, int l, bool full) {
-  const float a = __int2float_rn(acc);
-  const float b = __int2float_rn(l);
-  float qf;
-  if (full) {
-    asm("div.full.f32 %0, %1, %2;" : "=f"(qf) : "f"(a), "f"(b));
-  } else {
-    qf = __fdiv_rn(a, b);
-  }
+// Final division (qflash/kernel.py:176) with IEEE rounding, as the reference's
+// interpreted run computes it: int32(fp32(acc) / fp32(l)); a NaN or
+// out-of-range quotient becomes INT32_MIN (numpy's conversion on x86).
+__device__ __forceinline__ int div_ieee_to_i32(int acc, int l) {
+  const float qf = __fdiv_rn(__int2float_rn(acc), __int2float_rn(l));
   return (qf >= -2147483648.0f && qf < 2147483648.0f) ? __float2int_rz(qf) : (int)0x80000000;
 }
 
-// 32 int8 values (packed four per word) times o_scale, rounded to the output
+// NE int8 values (packed four per word) times o_scale, rounded to the output
 // dtype, stored at dst: o * o_scale as torch evaluates it (qflash/kernel.py:351),
 // the product in fp32 and one rounding to the dtype.
-__device__ __forceinline__ void store_dequant32(void* dst, const uint32_t (&res)[8], float os, int dtype, bool vec16) {
-  float f[32];
+template <int NE>
+__device__ __forceinline__ void store_dequant(void* dst, const uint32_t (&res)[NE / 4], float os, int dtype,
+                                              bool vec16) {
+  float f[NE];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) f[i] = (float)(int8_t)(res[i >> 2] >> (8 * (i & 3))) * os;
+  for (int i = 0; i < NE; ++i) f[i] = (float)(int8_t)(res[i >> 2] >> (8 * (i & 3))) * os;
   if (dtype == kF32) {
     float* d = (float*)dst;
     if (vec16) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) *(float4*)(d + 4 * i) = make_float4(f[4 * i], f[4 * i + 1], f[4 * i + 2], f[4 * i + 3]);
+      for (int i = 0; i < NE / 4; ++i)
+        *(float4*)(d + 4 * i) = make_float4(f[4 * i], f[4 * i + 1], f[4 * i + 2], f[4 * i + 3]);
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) d[i] = f[i];
+      for (int i = 0; i < NE; ++i) d[i] = f[i];
     }
   } else {
-    uint32_t w[16];
+    uint32_t w[NE / 2];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < NE / 2; ++i) {
       if (dtype == kF16) {
         const __half2 h2 = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
         w[i] = *(const uint32_t*)&h2;
@@ -193,12 +191,12 @@ __device__ __forceinline__ void store_dequant32(void* dst, const uint32_t (&res)
     }
     if (vec16) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < NE / 8; ++i)
         *(uint4*)((uint8_t*)dst + 16 * i) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
     } else {
       uint16_t* d = (uint16_t*)dst;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < NE / 2; ++i) {
         d[2 * i] = (uint16_t)w[i];
         d[2 * i + 1] = (uint16_t)(w[i] >> 16);
       }
@@ -238,24 +236,36 @@ struct Cfg {
   static constexpr int QA = DQK < 128 ? DQK : 128;  // bytes per row of one swizzle atom
   static constexpr int NQA = DQK / QA;              // atoms along the QK contraction
   static constexpr int VA = DV;                     // DV <= 128: one atom
+  static constexpr int S_COLS = 32 * SEGS;          // one S slot: a 32-column region per segment
+  // Paired accumulator (when it fits a 256-column TMEM allocation, so that two
+  // CTAs share an SM): acc element i of a row sits in TMEM column 2i, biased by
+  // 2^31, and column 2i + 1 holds the constant high word of 2^(52 + S), so the
+  // column pair reads as the double 2^(52+S) + (acc + 2^31) * 2^S and the
+  // fixed-point rescale is one FMA per element.  The PV MMA then multiplies by
+  // V2, V with a zero byte after every element (built in shared memory).
+  static constexpr bool ILV = 2 * S_COLS + SEGS * 2 * DV <= 256;
+  static constexpr int ACC_W = ILV ? 2 * DV : DV;   // TMEM columns of acc per segment
+  static constexpr int V2A = 2 * DV;                // bytes per key row of V2 (one swizzle atom)
   static constexpr int KVS = BIAS ? 4 : 8;          // K/V chunk stages
   static constexpr int Q_BYTES = kBM * DQK;
   static constexpr int K_SEG = kBN * DQK;
   static constexpr int V_SEG = kBN * DV;
+  static constexpr int V2_SEG = ILV ? kBN * V2A : 0;
   static constexpr int K_BYTES = SEGS * K_SEG;
   static constexpr int V_BYTES = SEGS * V_SEG;
+  static constexpr int V2_BYTES = SEGS * V2_SEG;
   static constexpr int B_BYTES = BIAS ? kBM * kBN * 4 : 0;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KVS * K_BYTES;
-  static constexpr int OFF_B = OFF_V + KVS * V_BYTES;
+  static constexpr int OFF_V2 = OFF_V + KVS * V_BYTES;
+  static constexpr int OFF_B = OFF_V2 + KVS * V2_BYTES;
   static constexpr int OFF_BAR = OFF_B + KVS * B_BYTES;
-  static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2;
+  static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2 + (ILV ? KVS : 0);
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
-  static constexpr int S_COLS = 32 * SEGS;           // one S slot: a 32-column region per segment
-  static constexpr int ACC_OFF = 2 * S_COLS;         // TMEM column of acc (DV columns per segment)
-  static constexpr int TMEM_NEED = ACC_OFF + SEGS * DV;
+  static constexpr int ACC_OFF = 2 * S_COLS;         // TMEM column of acc (ACC_W columns per segment)
+  static constexpr int TMEM_NEED = ACC_OFF + SEGS * ACC_W;
   static constexpr int TMEM_COLS = TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512);
   // resident CTAs the register budget is compiled for: what TMEM allows, at most
   // 2 (a third CTA per SM measured slower: the SM's shared units saturate first)
@@ -265,17 +275,23 @@ struct Cfg {
   static constexpr int REGS_FIT = (65536 / (MIN_CTAS * kThreads)) / 8 * 8 > 255 ? 255 : (65536 / (MIN_CTAS * kThreads)) / 8 * 8;
   static constexpr int MAX_REGS = (DQK == 64 && DV == 64 && SEGS == 1 && REGS_FIT > 144) ? 144 : REGS_FIT;
   static constexpr uint32_t IDESC_S = idesc_i8(kBM, kBN, false);
-  static constexpr uint32_t IDESC_PV = idesc_i8(kBM, DV, true);
+  static constexpr uint32_t IDESC_PV = idesc_i8(kBM, ILV ? V2A : DV, true);
   static constexpr uint32_t SWQ = QA == 32 ? kSw32 : (QA == 64 ? kSw64 : kSw128);
   static constexpr uint32_t SWV = VA == 32 ? kSw32 : (VA == 64 ? kSw64 : kSw128);
+  static constexpr uint32_t SWV2 = V2A == 64 ? kSw64 : kSw128;
 };
+
+// Position of 16-byte chunk c of row r in a tile of `w`-byte rows stored with
+// the w-byte TMA / UMMA swizzle (w = 32, 64, 128; tile base aligned to 8 * w):
+// the chunk index is XORed with bits [7, 7 + log2(w / 16)) of the row's offset.
+__device__ __forceinline__ int swz_chunk(int r, int c, int w) { return c ^ (((r * w) >> 7) & (w / 16 - 1)); }
 
 // MODE selects the arithmetic the kernel is compiled for:
 //   kGen      every QFLASH_* form, chosen at run time
 //   kFast     default arithmetic, 6-op exp2 proven exact for every chunk
 //   kChecked  default arithmetic, 6-op exp2 while the row max < m_lim, else the general form
 //   kPlain    default arithmetic, general exp2 (bias kernels: the score range is unknown)
-// Flags other than DIV_FULL must be 0 for every mode but kGen.
+// Flags other than DIV_FULL / DIV_IEEE must be 0 for every mode but kGen.
 enum Mode : int { kGen = 0, kFast = 1, kChecked = 2, kPlain = 3 };
 
 template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
@@ -313,6 +329,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
   auto s_full = [&](int i) { return bar0 + 8u * (4 + 2 * C::KVS + i); };
   auto p_full = [&](int i) { return bar0 + 8u * (6 + 2 * C::KVS + i); };
   auto acc_full = [&](int i) { return bar0 + 8u * (8 + 2 * C::KVS + i); };
+  auto v2_ready = [&](int i) { return bar0 + 8u * (10 + 2 * C::KVS + i); };
   uint32_t* tmem_slot = (uint32_t*)(smem + C::OFF_MISC);
   volatile int* abort_flag = (volatile int*)(smem + C::OFF_MISC + 4);
 
@@ -327,6 +344,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     for (int i = 0; i < C::KVS; ++i) {
       mbar_init(kv_full(i), 1);
       mbar_init(kv_empty(i), 1);
+      if (C::ILV) mbar_init(v2_ready(i), 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -388,51 +406,96 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
 
   if (warp == 4) {
     // ---------------------------------------------------------------- TMA producer
+    // Lane 0 issues the TMA loads.  With the paired accumulator the whole warp
+    // also builds V2 (V with a zero byte after every element) for each chunk,
+    // LAG chunks behind the loads, so V2 is ready well before its PV MMA.
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       if (BIAS) tma_prefetch_desc(&tmB);
-      uint32_t kv_it = 0;
-      int qi = 0;
-      bool ok = true;
-      for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k), ++qi) {
-        int nseg = 0;
-        for (int sg = 0; sg < SEGS; ++sg) {
-          int z, h, r0;
-          nseg += decode(item, sg, z, h, r0) ? 1 : 0;
-        }
-        const int qb = qi & 1;
-        if (!(ok = wait(q_empty(qb), ((qi >> 1) & 1) ^ 1, kErrQEmpty))) break;
-        mbar_arrive_expect_tx(q_full(qb), nseg * C::SEG_ROWS * DQK);
-        for (int sg = 0; sg < SEGS; ++sg) {
-          int z, h, r0;
-          if (!decode(item, sg, z, h, r0)) continue;
+    }
+    constexpr uint32_t LAG = C::KVS - 2;
+    // V2 of chunk `it`: lane r turns key row r of V (swizzled rows of DV bytes)
+    // into row r of V2 (swizzled rows of 2 DV bytes).
+    auto build_v2 = [&](uint32_t it) -> bool {
+      const int st = it % C::KVS;
+      const bool w_ok = wait(kv_full(st), (it / C::KVS) & 1, kErrV2Src);
+      if (!__all_sync(0xffffffffu, w_ok)) return false;
 #pragma unroll
-          for (int at = 0; at < C::NQA; ++at)
-            tma_load_4d(sbase + C::OFF_Q + qb * C::Q_BYTES + at * kBM * C::QA + sg * C::SEG_ROWS * C::QA, &tmQ,
-                        q_full(qb), at * C::QA, r0, h, z);
+      for (int sg = 0; sg < SEGS; ++sg) {
+        const uint32_t src = sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG + lane * DV;
+        const uint32_t dst = sbase + C::OFF_V2 + st * C::V2_BYTES + sg * C::V2_SEG + lane * C::V2A;
+#pragma unroll
+        for (int c = 0; c < DV / 16; ++c) {
+          const uint4 x = lds128(src + (swz_chunk(lane, c, DV) << 4));
+          sts128(dst + (swz_chunk(lane, 2 * c, C::V2A) << 4),
+                 make_uint4(__byte_perm(x.x, 0, 0x4140), __byte_perm(x.x, 0, 0x4342), __byte_perm(x.y, 0, 0x4140),
+                            __byte_perm(x.y, 0, 0x4342)));
+          sts128(dst + (swz_chunk(lane, 2 * c + 1, C::V2A) << 4),
+                 make_uint4(__byte_perm(x.z, 0, 0x4140), __byte_perm(x.z, 0, 0x4342), __byte_perm(x.w, 0, 0x4140),
+                            __byte_perm(x.w, 0, 0x4342)));
         }
-        for (int j = 0; j < nch; ++j, ++kv_it) {
-          const int st = kv_it % C::KVS;
-          if (!(ok = wait(kv_empty(st), ((kv_it / C::KVS) & 1) ^ 1, kErrKvEmpty))) break;
-          mbar_arrive_expect_tx(kv_full(st), nseg * (C::K_SEG + C::V_SEG + C::B_BYTES / SEGS));
+      }
+      fence_proxy_async_smem();  // the MMA reads V2 through the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(v2_ready(st));
+      return true;
+    };
+    uint32_t kv_it = 0, v2_it = 0;
+    int qi = 0;
+    bool ok = true;
+    for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k), ++qi) {
+      int nseg = 0;
+      for (int sg = 0; sg < SEGS; ++sg) {
+        int z, h, r0;
+        nseg += decode(item, sg, z, h, r0) ? 1 : 0;
+      }
+      const int qb = qi & 1;
+      bool ok0 = true;
+      if (lane == 0) {
+        if ((ok0 = wait(q_empty(qb), ((qi >> 1) & 1) ^ 1, kErrQEmpty))) {
+          mbar_arrive_expect_tx(q_full(qb), nseg * C::SEG_ROWS * DQK);
           for (int sg = 0; sg < SEGS; ++sg) {
             int z, h, r0;
             if (!decode(item, sg, z, h, r0)) continue;
 #pragma unroll
             for (int at = 0; at < C::NQA; ++at)
-              tma_load_4d(sbase + C::OFF_K + st * C::K_BYTES + sg * C::K_SEG + at * kBN * C::QA, &tmK, kv_full(st),
-                          at * C::QA, j * kBN, h, z);
-            tma_load_4d(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, &tmV, kv_full(st), a.v_col0, j * kBN,
-                        h, z);
-            if (BIAS)
-              tma_load_4d(sbase + C::OFF_B + st * C::B_BYTES + sg * C::SEG_ROWS * 128, &tmB, kv_full(st), j * kBN,
-                          r0, a.bias_hb ? h : 0, a.bias_zb ? (a.bias_zmod ? z % a.bias_zmod : z) : 0);
+              tma_load_4d(sbase + C::OFF_Q + qb * C::Q_BYTES + at * kBM * C::QA + sg * C::SEG_ROWS * C::QA, &tmQ,
+                          q_full(qb), at * C::QA, r0, h, z);
           }
         }
       }
+      if (!(ok = __shfl_sync(0xffffffffu, ok0, 0))) break;
+      for (int j = 0; j < nch; ++j, ++kv_it) {
+        if (C::ILV && kv_it >= LAG) {
+          if (!(ok = build_v2(v2_it))) break;
+          ++v2_it;
+        }
+        if (lane == 0) {
+          const int st = kv_it % C::KVS;
+          if ((ok0 = wait(kv_empty(st), ((kv_it / C::KVS) & 1) ^ 1, kErrKvEmpty))) {
+            mbar_arrive_expect_tx(kv_full(st), nseg * (C::K_SEG + C::V_SEG + C::B_BYTES / SEGS));
+            for (int sg = 0; sg < SEGS; ++sg) {
+              int z, h, r0;
+              if (!decode(item, sg, z, h, r0)) continue;
+#pragma unroll
+              for (int at = 0; at < C::NQA; ++at)
+                tma_load_4d(sbase + C::OFF_K + st * C::K_BYTES + sg * C::K_SEG + at * kBN * C::QA, &tmK,
+                            kv_full(st), at * C::QA, j * kBN, h, z);
+              tma_load_4d(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, &tmV, kv_full(st), a.v_col0,
+                          j * kBN, h, z);
+              if (BIAS)
+                tma_load_4d(sbase + C::OFF_B + st * C::B_BYTES + sg * C::SEG_ROWS * 128, &tmB, kv_full(st), j * kBN,
+                            r0, a.bias_hb ? h : 0, a.bias_zb ? (a.bias_zmod ? z % a.bias_zmod : z) : 0);
+            }
+          }
+        }
+        if (!(ok = __shfl_sync(0xffffffffu, ok0, 0))) break;
+      }
     }
+    if (C::ILV)
+      while (ok && v2_it < kv_it) ok = build_v2(v2_it++);
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -445,12 +508,18 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
         const int slot = gg & 1;
         const int st = gg % C::KVS;
         if (!wait(p_full(slot), (gg >> 1) & 1, kErrPFull)) return false;
+        if (C::ILV && !wait(v2_ready(st), (gg / C::KVS) & 1, kErrV2Ready)) return false;
         tc_fence_after();
 #pragma unroll
         for (int sg = 0; sg < SEGS; ++sg) {
+          // the paired accumulator starts each item from the pattern the softmax
+          // warps store, so its PV MMAs always accumulate
           const uint64_t bdesc =
-              smem_desc(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, kBN * C::VA, 8 * C::VA, C::SWV);
-          mma_i8_ts(tmem + C::ACC_OFF + sg * DV, tmem + slot * C::S_COLS, bdesc, C::IDESC_PV, init ? 0u : 1u);
+              C::ILV ? smem_desc(sbase + C::OFF_V2 + st * C::V2_BYTES + sg * C::V2_SEG, kBN * C::V2A, 8 * C::V2A,
+                                 C::SWV2)
+                     : smem_desc(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, kBN * C::VA, 8 * C::VA, C::SWV);
+          mma_i8_ts(tmem + C::ACC_OFF + sg * C::ACC_W, tmem + slot * C::S_COLS, bdesc, C::IDESC_PV,
+                    (C::ILV || !init) ? 1u : 0u);
         }
         tc_commit(acc_full(slot));
         tc_commit(kv_empty(st));
@@ -491,7 +560,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     const bool exp_idiv = GEN && (a.flags & QFLASH_FLAG_EXP_IDIV);
     const bool l_idiv = GEN && (a.flags & QFLASH_FLAG_L_IDIV);
     const bool acc_idiv = GEN && (a.flags & QFLASH_FLAG_ACC_IDIV);
-    const bool div_full = a.flags & QFLASH_FLAG_DIV_FULL;
+    const bool div_full = !(a.flags & QFLASH_FLAG_DIV_IEEE);
 
     const int rs = a.rs, eM = a.eM, rM = a.rM;
     const int S = a.as;
@@ -500,6 +569,16 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     const float ident_lim = (float)(1ull << (S - 1)) * 0.999f / (float)(delta0 < 0 ? -delta0 : (delta0 ? delta0 : 1));
     const float two_mS = __int_as_float((127 - S) << 23);  // 2^-S
     const float accM_ru = __ll2float_ru(a.accM < 0 ? -a.accM : a.accM);
+    // paired-accumulator constants (see rescale): H, the high word of 2^(52+S);
+    // 2^-S; 2^(52+S) + 2^(31+S); 2^(S-1); the range of A = alpha * acc_M for which
+    // the one-FMA rescale is exact (empty unless 1 <= S <= 32)
+    const uint32_t acc_hi = (uint32_t)(1075 + S) << 20;
+    const double two_mSd = __longlong_as_double((1023ll - S) << 52);
+    const double acc_anchor = __longlong_as_double(((1075ll + S) << 52) | (1ll << 31));
+    const double acc_half = __longlong_as_double((1022ll + S) << 52);
+    const bool s_pair = S >= 1 && S <= 32;
+    const long long acc_a_lo = s_pair ? (S > 20 ? (1ll << (S - 20)) : 1ll) : (1ll << 62);
+    const long long acc_a_hi = s_pair ? (2ll << S) - (S > 19 ? (1ll << (S - 19)) : 1ll) : 0ll;
     uint32_t g = 0;
     bool ok = true;
     for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k)) {
@@ -516,41 +595,102 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
       int m = kNegInf, l = 1;
       // upper bound on max |acc| of this row, kept in fp32 with round-up margins
       float abound = 0.f;
-      // acc lives in TMEM (this warp's lanes, DV columns); PV MMAs accumulate into it
-      const uint32_t acc_base = tmem + lane_base + C::ACC_OFF + sg * DV;
+      // acc lives in TMEM (this warp's lanes, ACC_W columns); PV MMAs accumulate into it
+      const uint32_t acc_base = tmem + lane_base + C::ACC_OFF + sg * C::ACC_W;
+      if (C::ILV && active) {
+        // paired accumulator: every item starts from acc = 0, i.e. (2^31, H) pairs;
+        // the stores complete (tcgen05.wait::st of the P store) before this
+        // warp releases the item's first P to the MMA warp
+        int pat[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pat[i] = (i & 1) ? (int)acc_hi : (int)0x80000000u;
+#pragma unroll
+        for (int part = 0; part < C::ACC_W / 32; ++part) tmem_st32(acc_base + part * 32, pat);
+      }
 
       // acc = rel(acc, alpha) in place, once PV_gg (the previous chunk's) has landed
       auto rescale = [&](uint32_t gg, int alpha, long long A) -> bool {
         if (!wait(acc_full(gg & 1), (gg >> 1) & 1, kErrPvFull)) return false;
         tc_fence_after();
-        const bool fast = !acc_idiv && S >= 13 && A >= 0 && A < (1ll << 31);
-        if (__all_sync(0xffffffffu, fast || !row_ok)) {
-          // int32((x * A + 2^(S-1)) >> S) on the FP64 pipe (rel_fp64)
-          const double Ad = (double)A;
-          const double Cd = __longlong_as_double(((1023ll + 51 + S) << 52) | (1ll << 51) | 1ll);
+        if constexpr (C::ILV) {
+          // Paired accumulator: column pair (u, H) with u = x + 2^31 reads as the
+          // double X = 2^(52+S) + u * 2^S.  With Ad = A * 2^-S and
+          // Cd = 2^(52+S) + 2^(31+S) + 2^(S-1) - (2^52 + 2^31) * A,
+          // X * Ad + Cd = x*A + 2^(S-1) + 2^(31+S) + 2^(52+S) exactly, which lies in
+          // [2^(52+S), 2^(53+S)) (ulp 2^S) while |rel(x)| < 2^31; one FMA rounded
+          // down therefore gives 2^(52+S) + 2^S * (2^31 + rel(x)): its low word is
+          // the biased new acc and its high word is H again.  Ad is exact; Cd is
+          // exact (a multiple of 2^(S-1) below 2^(52+S) in magnitude) for A in
+          // [acc_a_lo, acc_a_hi); the first step forms Cd - 2^(S-1) exactly with an
+          // FMA ((2^21 + 1) (2^S - A) 2^31, a 53-bit multiple of 2^31).  A = 0
+          // (alpha = 0: the row max jumped far) makes every rel(x) 0: Ad = 0 and
+          // Cd = 2^(52+S) + 2^(31+S) give exactly that.
+          const double Af = (double)A;
+          const bool fast = !acc_idiv && (A == 0 || (A >= acc_a_lo && A < acc_a_hi && abound * (float)Af * two_mS < 2.0e9f));
+          if (__all_sync(0xffffffffu, fast || !row_ok)) {
+            const double Ad = Af * two_mSd;
+            const double Cd = A == 0 ? acc_anchor : __fma_rn(-4503601774854144.0, Af, acc_anchor) + acc_half;
 #pragma unroll
-          for (int part = 0; part < DV / 32; ++part) {
-            int v[32];
-            tmem_ld32(acc_base + part * 32, v);
+            for (int part = 0; part < C::ACC_W / 32; ++part) {
+              int v[32];
+              tmem_ld32(acc_base + part * 32, v);
 #pragma unroll
-            for (int d = 0; d < 32; ++d) v[d] = rel_fp64(v[d], Ad, Cd);
-            tmem_st32(acc_base + part * 32, v);
+              for (int d = 0; d < 16; ++d) {
+                const double y = __fma_rd(__hiloint2double(v[2 * d + 1], v[2 * d]), Ad, Cd);
+                v[2 * d] = __double2loint(y);
+                v[2 * d + 1] = __double2hiint(y);
+              }
+              tmem_st32(acc_base + part * 32, v);
+            }
+          } else {
+            // the general forms (64-bit product, idiv, shifts outside [1, 32]) are
+            // rare: a compact loop over the pairs that takes v[0] and rotates
+#pragma unroll 1
+            for (int part = 0; part < C::ACC_W / 32; ++part) {
+              int v[32];
+              tmem_ld32(acc_base + part * 32, v);
+#pragma unroll 1
+              for (int d = 0; d < 16; ++d) {
+                const int x = v[0] ^ (int)0x80000000u;
+                const int r = acc_idiv ? rel_idiv(x, alpha, rs) : rel_shift64(x, (unsigned long long)A, S);
+#pragma unroll
+                for (int i = 0; i < 30; ++i) v[i] = v[i + 2];
+                v[30] = r ^ (int)0x80000000u;
+                v[31] = (int)acc_hi;
+              }
+              tmem_st32(acc_base + part * 32, v);
+            }
           }
         } else {
-          // the general forms (64-bit product, idiv) are rare: a compact loop
-          // that takes v[0] and rotates the array
-#pragma unroll 1
-          for (int part = 0; part < DV / 32; ++part) {
-            int v[32];
-            tmem_ld32(acc_base + part * 32, v);
-#pragma unroll 1
-            for (int d = 0; d < 32; ++d) {
-              const int r = acc_idiv ? rel_idiv(v[0], alpha, rs) : rel_shift64(v[0], (unsigned long long)A, S);
+          const bool fast = !acc_idiv && S >= 13 && A >= 0 && A < (1ll << 31);
+          if (__all_sync(0xffffffffu, fast || !row_ok)) {
+            // int32((x * A + 2^(S-1)) >> S) on the FP64 pipe (rel_fp64)
+            const double Ad = (double)A;
+            const double Cd = __longlong_as_double(((1023ll + 51 + S) << 52) | (1ll << 51) | 1ll);
 #pragma unroll
-              for (int i = 0; i < 31; ++i) v[i] = v[i + 1];
-              v[31] = r;
+            for (int part = 0; part < DV / 32; ++part) {
+              int v[32];
+              tmem_ld32(acc_base + part * 32, v);
+#pragma unroll
+              for (int d = 0; d < 32; ++d) v[d] = rel_fp64(v[d], Ad, Cd);
+              tmem_st32(acc_base + part * 32, v);
             }
-            tmem_st32(acc_base + part * 32, v);
+          } else {
+            // the general forms (64-bit product, idiv) are rare: a compact loop
+            // that takes v[0] and rotates the array
+#pragma unroll 1
+            for (int part = 0; part < DV / 32; ++part) {
+              int v[32];
+              tmem_ld32(acc_base + part * 32, v);
+#pragma unroll 1
+              for (int d = 0; d < 32; ++d) {
+                const int r = acc_idiv ? rel_idiv(v[0], alpha, rs) : rel_shift64(v[0], (unsigned long long)A, S);
+#pragma unroll
+                for (int i = 0; i < 31; ++i) v[i] = v[i + 1];
+                v[31] = r;
+              }
+              tmem_st32(acc_base + part * 32, v);
+            }
           }
         }
         tmem_wait_st();
@@ -582,16 +722,14 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
 #pragma unroll
             for (int c = 0; c < 32; ++c) s[c] = c < nvalid ? s[c] : kNegInf;
           }
-          // row max as a tree (depth 5)
-          int t16[16];
+          // row max (with the running max m) as a tree of three-input maxima
+          int t3[11];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) t16[c] = max(s[c], s[c + 16]);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) t16[c] = max(t16[c], t16[c + 8]);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) t16[c] = max(t16[c], t16[c + 4]);
-          const int mx = max(max(t16[0], t16[2]), max(t16[1], t16[3]));
-          m_new = max(m, mx);
+          for (int c = 0; c < 10; ++c) t3[c] = __vimax3_s32(s[3 * c], s[3 * c + 1], s[3 * c + 2]);
+          t3[10] = max(s[30], s[31]);
+          m_new = max(__vimax3_s32(__vimax3_s32(t3[0], t3[1], t3[2]), __vimax3_s32(t3[3], t3[4], t3[5]),
+                                   __vimax3_s32(t3[6], t3[7], t3[8])),
+                      __vimax3_s32(t3[9], t3[10], m));
           bool use_fast = MODE == kFast;
           if (MODE == kChecked) use_fast = __all_sync(0xffffffffu, m_new < a.m_lim);
           // In a ragged last chunk every padded column holds NEG_INF, so all of
@@ -703,61 +841,77 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
         if (!(ok = wait(acc_full((g - 1) & 1), ((g - 1) >> 1) & 1, kErrPvFull))) break;
         tc_fence_after();
         int8_t* orow = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row * a.os_n + a.v_col0;
-        // Exact shortcut: for |acc| < 2^23 and 0 < l < 2^24, trunc(RN_f32(acc / l))
-        // equals the truncated integer quotient (rounding up to an integer n >= 2
-        // needs l >= 2^24 / n, i.e. |acc| >= 2^23).  That quotient is
-        // floor(|acc| * RU(1/l)) taken with one round-toward-zero FMA:
-        // RU(1/l) - 1/l < 2^-23 / l, so |acc| * RU(1/l) lies in
-        // [|acc| / l, |acc| / l + 1/l), below the next integer.
-        const bool fast_div = !div_full && l > 0 && l < (1 << 24) && abound < 8388607.f;
-        const bool fastw = __all_sync(0xffffffffu, fast_div || !row_ok);
-        const float rcp = __frcp_ru((float)l);
+        constexpr int EPP = C::ILV ? 16 : 32;  // acc elements per 32-column TMEM load
+        constexpr int STEP = C::ILV ? 2 : 1;   // register stride of the elements
+        // Default rounding: the reference's compiled sequence itself -- the int32
+        // to fp32 conversion, div.full.f32 and the truncating, saturating
+        // conversion back (cvt.rzi.s32.f32) -- for every element.
+        // IEEE rounding (QFLASH_FLAG_DIV_IEEE): for |acc| < 2^23 and 0 < l < 2^24,
+        // trunc(RN_f32(acc / l)) equals the truncated integer quotient (rounding up
+        // to an integer n >= 2 needs l >= 2^24 / n, i.e. |acc| >= 2^23), which is
+        // trunc(RZ(fp32(acc) * RU(1/l))): RU(1/l) - 1/l < 2^-23 / l, so
+        // |acc| * RU(1/l) lies in [|acc| / l, |acc| / l + 1/l), below the next
+        // integer, and rounding toward zero cannot drop below the integer part.
+        const float lf = __int2float_rn(l);
+        const bool fast_ieee =
+            __all_sync(0xffffffffu, (l > 0 && l < (1 << 24) && abound < 8388607.f) || !row_ok);
+        const float rcp = __frcp_ru(lf);
 #pragma unroll
-        for (int part = 0; part < DV / 32; ++part) {
+        for (int part = 0; part < C::ACC_W / 32; ++part) {
           int v[32];
           tmem_ld32(acc_base + part * 32, v);
-          uint32_t res[8];
-          if (fastw) {
+          if (C::ILV) {
 #pragma unroll
-            for (int w4 = 0; w4 < 8; ++w4) {
-              int r4[4];
+            for (int i = 0; i < 16; ++i) v[2 * i] ^= (int)0x80000000u;  // unbias
+          }
+          uint32_t res[EPP / 4];
+          if (div_full || fast_ieee) {
+            int r[EPP];
 #pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const int x = v[w4 * 4 + b];
-                const int ux = abs(x);
-                const float af = __int_as_float(ux | 0x4B000000) - 8388608.0f;
-                const int qd = __float_as_int(__fmaf_rz(af, rcp, 8388608.0f)) - 0x4B000000;
-                r4[b] = x < 0 ? -qd : qd;
+            for (int i = 0; i < EPP; ++i) {
+              const float xf = __int2float_rn(v[STEP * i]);
+              float qf;
+              if (div_full) {
+                asm("div.full.f32 %0, %1, %2;" : "=f"(qf) : "f"(xf), "f"(lf));
+              } else {
+                qf = __fmul_rz(xf, rcp);
               }
-              res[w4] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
+              r[i] = __float2int_rz(qf);
             }
+#pragma unroll
+            for (int w4 = 0; w4 < EPP / 4; ++w4)
+              res[w4] = __byte_perm(__byte_perm(r[4 * w4], r[4 * w4 + 1], 0x0040),
+                                    __byte_perm(r[4 * w4 + 2], r[4 * w4 + 3], 0x0040), 0x5410);
           } else {
-            // rare: the literal fp32 division, compact (v[0..3] per step, rotating)
+            // rare: the IEEE fp32 division, compact (4 elements per step, rotating)
 #pragma unroll 1
-            for (int w4 = 0; w4 < 8; ++w4) {
+            for (int w4 = 0; w4 < EPP / 4; ++w4) {
               int r4[4];
 #pragma unroll
-              for (int b = 0; b < 4; ++b) r4[b] = div_to_i32(v[b], l, div_full);
+              for (int b = 0; b < 4; ++b) r4[b] = div_ieee_to_i32(v[STEP * b], l);
 #pragma unroll
-              for (int i = 0; i < 28; ++i) v[i] = v[i + 4];
+              for (int i = 0; i < 32 - 4 * STEP; ++i) v[i] = v[i + 4 * STEP];
 #pragma unroll
-              for (int i = 0; i < 7; ++i) res[i] = res[i + 1];
-              res[7] = __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
+              for (int i = 0; i < EPP / 4 - 1; ++i) res[i] = res[i + 1];
+              res[EPP / 4 - 1] =
+                  __byte_perm(__byte_perm(r4[0], r4[1], 0x0040), __byte_perm(r4[2], r4[3], 0x0040), 0x5410);
             }
           }
           if (row_ok && a.out) {
             const int esz = a.out_dtype == kF32 ? 4 : 2;
             uint8_t* drow = (uint8_t*)a.out +
                             ((long long)z * a.ou_z + (long long)h * a.ou_h + (long long)row * a.ou_n + a.v_col0 +
-                             part * 32) * esz;
-            store_dequant32(drow, res, a.o_scale, a.out_dtype, a.out_vec16);
+                             part * EPP) * esz;
+            store_dequant<EPP>(drow, res, a.o_scale, a.out_dtype, a.out_vec16);
           } else if (row_ok) {
             if (a.o_vec16) {
-              *(int4*)(orow + part * 32) = make_int4((int)res[0], (int)res[1], (int)res[2], (int)res[3]);
-              *(int4*)(orow + part * 32 + 16) = make_int4((int)res[4], (int)res[5], (int)res[6], (int)res[7]);
+#pragma unroll
+              for (int q4 = 0; q4 < EPP / 16; ++q4)
+                *(int4*)(orow + part * EPP + 16 * q4) = make_int4((int)res[4 * q4], (int)res[4 * q4 + 1],
+                                                                   (int)res[4 * q4 + 2], (int)res[4 * q4 + 3]);
             } else {
 #pragma unroll
-              for (int b = 0; b < 32; ++b) orow[part * 32 + b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
+              for (int b = 0; b < EPP; ++b) orow[part * EPP + b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
             }
           }
         }
@@ -982,6 +1136,11 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
   if (!dparams && sm_rscale <= 0) return set_err(QFLASH_ERR_ARG, "sm_rscale must be positive");
   if (l_shift < 1 || l_shift > 62 || acc_shift < 1 || acc_shift > 62) return set_err(QFLASH_ERR_ARG, "shift out of [1, 62]");
   if (bias && !bias_strides) return set_err(QFLASH_ERR_ARG, "bias without strides");
+  if ((flags & QFLASH_FLAG_DIV_FULL) && (flags & QFLASH_FLAG_DIV_IEEE))
+    return set_err(QFLASH_ERR_ARG, "QFLASH_FLAG_DIV_FULL and QFLASH_FLAG_DIV_IEEE are exclusive");
+  if (flags & ~(QFLASH_FLAG_EXP_IDIV | QFLASH_FLAG_L_IDIV | QFLASH_FLAG_ACC_IDIV | QFLASH_FLAG_DIV_FULL |
+                QFLASH_FLAG_DIV_IEEE))
+    return set_err(QFLASH_ERR_ARG, "unknown flag bits 0x%x", flags);
   int dev = 0;
   if (int rc0 = select_device(q, &dev)) return rc0;
 

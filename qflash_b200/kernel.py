@@ -13,10 +13,11 @@ QFLASH_EXP_USE_SHIFT, QFLASH_L_USE_SHIFT, QFLASH_ACC_USE_SHIFT (default 1),
 QFLASH_L_SHIFT, QFLASH_ACC_SHIFT (default 30).  QFLASH_AUTOTUNE and
 QFLASH_CUDA_GRAPH are accepted; they only pick Triton launch configurations
 there and change no arithmetic, and this kernel has a single configuration.
-QFLASH_DIV selects the rounding of the final fp32 division acc / l:
-"ieee" (default; the reference's integer path as specified and as its
-interpreted run computes it) or "full" (the approximate fp32 divide that the
-reference's compiled GPU kernel uses).  QFLASH_FUSED=1 routes qflash.forward
+QFLASH_DIV selects the rounding of the final fp32 division acc / l
+(kernel.py:176): "full" (default; the approximate fp32 divide div.full.f32 that
+the reference's compiled Triton kernel uses on B200, so the output is bit for
+bit what the reference produces there) or "ieee" (IEEE round-to-nearest, as the
+reference's interpreted run computes it).  QFLASH_FUSED=1 routes qflash.forward
 (output mode) through ``forward_fused``: the same result without the host
 synchronisation; inputs for which the reference raises (all-zero q or k)
 then give an all-NaN output instead of an exception.
@@ -37,7 +38,7 @@ L_USE_SHIFT = os.environ.get("QFLASH_L_USE_SHIFT", "1") == "1"
 ACC_USE_SHIFT = os.environ.get("QFLASH_ACC_USE_SHIFT", "1") == "1"
 L_SHIFT = int(os.environ.get("QFLASH_L_SHIFT", "30"))
 ACC_SHIFT = int(os.environ.get("QFLASH_ACC_SHIFT", "30"))
-DIV_MODE = os.environ.get("QFLASH_DIV", "ieee")
+DIV_MODE = os.environ.get("QFLASH_DIV", "full")
 # qflash.forward runs every step on the device (forward_fused) unless
 # QFLASH_FUSED=0 selects the torch-op host path (the reference's own sequence)
 FUSED = os.environ.get("QFLASH_FUSED", "1") == "1"
@@ -59,8 +60,8 @@ def arith_flags(exp_use_shift=None, l_use_shift=None, acc_use_shift=None, div_mo
     mode = DIV_MODE if div_mode is None else div_mode
     if mode not in ("ieee", "full"):
         raise ValueError(f"QFLASH_DIV must be 'ieee' or 'full', got {mode!r}")
-    if mode == "full":
-        f |= _lib.FLAG_DIV_FULL
+    if mode == "ieee":
+        f |= _lib.FLAG_DIV_IEEE
     return f
 
 

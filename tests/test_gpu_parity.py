@@ -52,18 +52,47 @@ def test_rows_per_item_forced(golden, name, rpi, monkeypatch):
     assert mism == 0, f"{mism} of {o.size} int8 outputs differ"
 
 
-@pytest.mark.parametrize("name", ["cfg1_vit_s", "cfg3_deit_t", "bench_a2_fp16", "n80_d256"])
+def _triton_gpu(name):
+    with np.load(__import__("conftest").GOLDEN / "triton_gpu" / f"{name}.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.mark.parametrize("name", ["cfg1_vit_s", "cfg2_vit_b", "cfg3_deit_t", "cfg5_vit_l", "bench_a2_fp16",
+                                  "bench_a7_fp16", "n80_d256", "n197_d128", "strided_qattn", "bool_mask",
+                                  "bool_mask_full_row", "float_mask_m100", "cfg4_swin_s1", "cfg4_swin_s4"])
 def test_forward_end_to_end(golden, name):
-    """qflash.forward on the float inputs: same int8 output, same returned values."""
+    """The public qflash.forward (on-device path, default final division) on the
+    float inputs returns exactly what the reference's compiled Triton kernel
+    returns on B200: o8 * o_scale with o8 from tests/golden/triton_gpu (for the
+    masked cases the bias is built on the device, as the reference builds it
+    on CUDA)."""
     import qflash
     rec = golden(name)
+    gpu = _triton_gpu(name)
     q, k, v = (torch.from_numpy(rec[x]).cuda() for x in "qkv")
     mask = torch.from_numpy(rec["mask"]).cuda() if "mask" in rec else None
     s = float(rec["scale"])
     out = qflash.qflash.forward(q, k, v, attn_mask=mask, scale=None if np.isnan(s) else s)
     assert out.dtype == q.dtype and out.shape == q.shape
     o_scale = v.abs().amax() / 127
-    expect = torch.from_numpy(rec["o8"]).cuda() * o_scale
+    expect = torch.from_numpy(gpu["o8"]).cuda() * o_scale
+    mism = int((out != expect).sum())
+    assert mism == 0, f"{mism} of {out.numel()} outputs differ from the compiled reference"
+
+
+@pytest.mark.parametrize("name", ["cfg1_vit_s", "bench_a2_fp16", "bool_mask", "cfg4_swin_s1"])
+def test_forward_host_path_end_to_end(golden, name, monkeypatch):
+    """The torch-op host path of qflash.forward (QFLASH_FUSED=0) gives the same."""
+    import qflash
+    from qflash_b200 import kernel as K
+    monkeypatch.setattr(K, "FUSED", False)
+    rec = golden(name)
+    gpu = _triton_gpu(name)
+    q, k, v = (torch.from_numpy(rec[x]).cuda() for x in "qkv")
+    mask = torch.from_numpy(rec["mask"]).cuda() if "mask" in rec else None
+    s = float(rec["scale"])
+    out = qflash.qflash.forward(q, k, v, attn_mask=mask, scale=None if np.isnan(s) else s)
+    expect = torch.from_numpy(gpu["o8"]).cuda() * (v.abs().amax() / 127)
     assert torch.equal(out, expect)
 
 
@@ -75,21 +104,47 @@ def test_device_error_word_clear():
 TRITON_GPU = sorted(p.stem for p in (__import__("conftest").GOLDEN / "triton_gpu").glob("*.npz"))
 
 
+@pytest.mark.parametrize("explicit", [False, True])
 @pytest.mark.parametrize("name", TRITON_GPU)
-def test_div_full_matches_compiled_reference_on_b200(golden, name):
-    """QFLASH_DIV=full reproduces the reference's compiled Triton kernel on B200
+def test_default_division_matches_compiled_reference_on_b200(golden, name, explicit):
+    """The default final division (flags 0, or QFLASH_FLAG_DIV_FULL given
+    explicitly) reproduces the reference's compiled Triton kernel on B200
     (approximate fp32 divide), captured by tests/golden/gen_golden_triton_gpu.py."""
-    import numpy as np
+    from qflash_b200 import _lib
     from qflash_b200 import kernel as K
     rec = dict(golden(name))
-    with np.load(__import__("conftest").GOLDEN / "triton_gpu" / f"{name}.npz") as z:
-        gpu = {k: z[k] for k in z.files}
+    gpu = _triton_gpu(name)
     if "bias" in gpu:
         rec["bias"] = gpu["bias"]          # the GPU host path's bias (reciprocal-multiply rounding)
     e, l, a, _, _ = (int(x) for x in rec["flags"])
-    o = _run_kernel(rec, flags=K.arith_flags(bool(e), bool(l), bool(a), "full"))
+    flags = K.arith_flags(bool(e), bool(l), bool(a), "full") | (_lib.FLAG_DIV_FULL if explicit else 0)
+    o = _run_kernel(rec, flags=flags)
     mism = int((o != gpu["o8"]).sum())
     assert mism == 0, f"{mism} of {o.size} int8 outputs differ from the compiled reference"
+
+
+@pytest.mark.parametrize("rpi", ["32", "64"])
+@pytest.mark.parametrize("name", ["cfg2_vit_b", "cfg5_vit_l", "bool_mask", "n65_d32"])
+def test_default_division_small_items(golden, name, rpi, monkeypatch):
+    """Same, with the small work items that small grids use."""
+    from qflash_b200 import kernel as K
+    monkeypatch.setenv("QFLASH_ROWS_PER_ITEM", rpi)
+    rec = dict(golden(name))
+    gpu = _triton_gpu(name)
+    if "bias" in gpu:
+        rec["bias"] = gpu["bias"]
+    e, l, a, _, _ = (int(x) for x in rec["flags"])
+    o = _run_kernel(rec, flags=K.arith_flags(bool(e), bool(l), bool(a), "full"))
+    assert int((o != gpu["o8"]).sum()) == 0
+
+
+def test_conflicting_division_flags_rejected():
+    from qflash_b200 import _lib
+    from qflash_b200 import kernel as K
+    x = torch.zeros(1, 1, 32, 32, dtype=torch.int8, device="cuda")
+    with pytest.raises(RuntimeError, match="exclusive"):
+        K.launch_int8(x, x, x, torch.empty_like(x), 4033, -16, 2064, 266239, 266239,
+                      flags=_lib.FLAG_DIV_FULL | _lib.FLAG_DIV_IEEE)
 
 
 def test_bounded_wait_reports_timeout_and_context_stays_usable():

@@ -47,9 +47,10 @@ def test_quantize_bias_matches_reference_cpu(golden, name):
 
 
 def test_arith_flags():
-    assert K.arith_flags(True, True, True, "ieee") == 0
-    assert K.arith_flags(False, True, True, "ieee") == 1
-    assert K.arith_flags(True, False, False, "full") == 2 | 4 | 8
+    assert K.arith_flags(True, True, True, "full") == 0          # the reference as compiled on B200
+    assert K.arith_flags(True, True, True, "ieee") == 16
+    assert K.arith_flags(False, True, True, "ieee") == 1 | 16
+    assert K.arith_flags(True, False, False, "full") == 2 | 4
     with pytest.raises(ValueError):
         K.arith_flags(div_mode="fast")
 
