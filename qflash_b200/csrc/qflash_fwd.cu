@@ -51,8 +51,7 @@ __device__ unsigned int g_err;       // set when a bounded wait gives up
 
 // Error codes written to g_err (bit set per site).
 enum : unsigned { kErrQEmpty = 1, kErrKvEmpty = 2, kErrQFull = 4, kErrKvFull = 8, kErrPFull = 16,
-                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128, kErrV2Ready = 256, kErrV2Src = 512,
-                  kErrSelftest = 1u << 31 };
+                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128, kErrSelftest = 1u << 31 };
 
 struct KArgs {
   int Z, H, N, nch, ntiles, nitems, ZH;
@@ -261,7 +260,8 @@ struct Cfg {
   static constexpr int OFF_V2 = OFF_V + KVS * V_BYTES;
   static constexpr int OFF_B = OFF_V2 + KVS * V2_BYTES;
   static constexpr int OFF_BAR = OFF_B + KVS * B_BYTES;
-  static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2 + (ILV ? KVS : 0);
+  static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2;
+  static constexpr int THREADS = kThreads;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr int ACC_OFF = 2 * S_COLS;         // TMEM column of acc (ACC_W columns per segment)
@@ -270,9 +270,9 @@ struct Cfg {
   // resident CTAs the register budget is compiled for: what TMEM allows, at most
   // 2 (a third CTA per SM measured slower: the SM's shared units saturate first)
   static constexpr int MIN_CTAS = (512 / TMEM_COLS) < 2 ? (512 / TMEM_COLS) : 2;
-  // registers per thread for MIN_CTAS CTAs of kThreads threads (multiple of 8);
+  // registers per thread for MIN_CTAS CTAs of THREADS threads (multiple of 8);
   // the d = 64 one-head-per-tile kernels (ViT, DeiT) measured fastest at 144
-  static constexpr int REGS_FIT = (65536 / (MIN_CTAS * kThreads)) / 8 * 8 > 255 ? 255 : (65536 / (MIN_CTAS * kThreads)) / 8 * 8;
+  static constexpr int REGS_FIT = (65536 / (MIN_CTAS * THREADS)) / 8 * 8 > 255 ? 255 : (65536 / (MIN_CTAS * THREADS)) / 8 * 8;
   static constexpr int MAX_REGS = (DQK == 64 && DV == 64 && SEGS == 1 && REGS_FIT > 144) ? 144 : REGS_FIT;
   static constexpr uint32_t IDESC_S = idesc_i8(kBM, kBN, false);
   static constexpr uint32_t IDESC_PV = idesc_i8(kBM, ILV ? V2A : DV, true);
@@ -295,7 +295,7 @@ __device__ __forceinline__ int swz_chunk(int r, int c, int w) { return c ^ (((r 
 enum Mode : int { kGen = 0, kFast = 1, kChecked = 2, kPlain = 3 };
 
 template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
-__global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS>::MAX_REGS))
+__global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS>::MAX_REGS))
     qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
                    const KArgs a_in) {
@@ -329,7 +329,6 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
   auto s_full = [&](int i) { return bar0 + 8u * (4 + 2 * C::KVS + i); };
   auto p_full = [&](int i) { return bar0 + 8u * (6 + 2 * C::KVS + i); };
   auto acc_full = [&](int i) { return bar0 + 8u * (8 + 2 * C::KVS + i); };
-  auto v2_ready = [&](int i) { return bar0 + 8u * (10 + 2 * C::KVS + i); };
   uint32_t* tmem_slot = (uint32_t*)(smem + C::OFF_MISC);
   volatile int* abort_flag = (volatile int*)(smem + C::OFF_MISC + 4);
 
@@ -344,7 +343,6 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     for (int i = 0; i < C::KVS; ++i) {
       mbar_init(kv_full(i), 1);
       mbar_init(kv_empty(i), 1);
-      if (C::ILV) mbar_init(v2_ready(i), 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -406,22 +404,93 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
 
   if (warp == 4) {
     // ---------------------------------------------------------------- TMA producer
-    // Lane 0 issues the TMA loads.  With the paired accumulator the whole warp
-    // also builds V2 (V with a zero byte after every element) for each chunk,
-    // LAG chunks behind the loads, so V2 is ready well before its PV MMA.
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       if (BIAS) tma_prefetch_desc(&tmB);
+      uint32_t kv_it = 0;
+      int qi = 0;
+      bool ok = true;
+      for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k), ++qi) {
+        // per segment: head (z, h), first query row, bias batch index; -1 = empty
+        int sz[SEGS], sh[SEGS], sr[SEGS], sbz[SEGS];
+        int nseg = 0;
+#pragma unroll
+        for (int sg = 0; sg < SEGS; ++sg) {
+          if (decode(item, sg, sz[sg], sh[sg], sr[sg])) {
+            ++nseg;
+            sbz[sg] = a.bias_zb ? (a.bias_zmod ? sz[sg] % a.bias_zmod : sz[sg]) : 0;
+          } else {
+            sz[sg] = -1;
+          }
+        }
+        const int qb = qi & 1;
+        if (!(ok = wait(q_empty(qb), ((qi >> 1) & 1) ^ 1, kErrQEmpty))) break;
+        mbar_arrive_expect_tx(q_full(qb), nseg * C::SEG_ROWS * DQK);
+#pragma unroll
+        for (int sg = 0; sg < SEGS; ++sg) {
+          if (sz[sg] < 0) continue;
+#pragma unroll
+          for (int at = 0; at < C::NQA; ++at)
+            tma_load_4d(sbase + C::OFF_Q + qb * C::Q_BYTES + at * kBM * C::QA + sg * C::SEG_ROWS * C::QA, &tmQ,
+                        q_full(qb), at * C::QA, sr[sg], sh[sg], sz[sg]);
+        }
+        for (int j = 0; j < nch; ++j, ++kv_it) {
+          const int st = kv_it % C::KVS;
+          if (!(ok = wait(kv_empty(st), ((kv_it / C::KVS) & 1) ^ 1, kErrKvEmpty))) break;
+          mbar_arrive_expect_tx(kv_full(st), nseg * (C::K_SEG + C::V_SEG + C::B_BYTES / SEGS));
+#pragma unroll
+          for (int sg = 0; sg < SEGS; ++sg) {
+            if (sz[sg] < 0) continue;
+#pragma unroll
+            for (int at = 0; at < C::NQA; ++at)
+              tma_load_4d(sbase + C::OFF_K + st * C::K_BYTES + sg * C::K_SEG + at * kBN * C::QA, &tmK, kv_full(st),
+                          at * C::QA, j * kBN, sh[sg], sz[sg]);
+            tma_load_4d(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, &tmV, kv_full(st), a.v_col0, j * kBN,
+                        sh[sg], sz[sg]);
+            if (BIAS)
+              tma_load_4d(sbase + C::OFF_B + st * C::B_BYTES + sg * C::SEG_ROWS * 128, &tmB, kv_full(st), j * kBN,
+                          sr[sg], a.bias_hb ? sh[sg] : 0, sbz[sg]);
+          }
+        }
+      }
     }
-    constexpr uint32_t LAG = C::KVS - 2;
-    // V2 of chunk `it`: lane r turns key row r of V (swizzled rows of DV bytes)
-    // into row r of V2 (swizzled rows of 2 DV bytes).
-    auto build_v2 = [&](uint32_t it) -> bool {
-      const int st = it % C::KVS;
-      const bool w_ok = wait(kv_full(st), (it / C::KVS) & 1, kErrV2Src);
-      if (!__all_sync(0xffffffffu, w_ok)) return false;
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    // Lane 0 issues the MMAs.  With the paired accumulator all 32 lanes also
+    // build V2 of each chunk (V with a zero byte after every element) once its
+    // S MMA and the previous chunk's PV MMA are issued, so the build is off the
+    // softmax -> PV -> rescale path; PV of the chunk is issued one step later.
+    uint32_t g = 0;
+    int qi = 0;
+    bool ok = true;
+    // acc (+)= P_gg V_gg straight into the TMEM accumulator, once the softmax
+    // warps have written P_gg and rescaled acc; `init` starts a new item (lane 0)
+    auto issue_pv = [&](uint32_t gg, bool init) -> bool {
+      const int slot = gg & 1;
+      const int st = gg % C::KVS;
+      if (!wait(p_full(slot), (gg >> 1) & 1, kErrPFull)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int sg = 0; sg < SEGS; ++sg) {
+        // the paired accumulator starts each item from the pattern the softmax
+        // warps store, so its PV MMAs always accumulate
+        const uint64_t bdesc =
+            C::ILV ? smem_desc(sbase + C::OFF_V2 + st * C::V2_BYTES + sg * C::V2_SEG, kBN * C::V2A, 8 * C::V2A,
+                               C::SWV2)
+                   : smem_desc(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, kBN * C::VA, 8 * C::VA, C::SWV);
+        mma_i8_ts(tmem + C::ACC_OFF + sg * C::ACC_W, tmem + slot * C::S_COLS, bdesc, C::IDESC_PV,
+                  (C::ILV || !init) ? 1u : 0u);
+      }
+      tc_commit(acc_full(slot));
+      tc_commit(kv_empty(st));
+      return true;
+    };
+    // V2 of stage st: lane r turns key row r of V (swizzled rows of DV bytes)
+    // into row r of V2 (swizzled rows of 2 DV bytes), then makes it visible to
+    // the tensor core (async proxy)
+    auto build_v2 = [&](int st) {
 #pragma unroll
       for (int sg = 0; sg < SEGS; ++sg) {
         const uint32_t src = sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG + lane * DV;
@@ -437,102 +506,22 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
                             __byte_perm(x.w, 0, 0x4342)));
         }
       }
-      fence_proxy_async_smem();  // the MMA reads V2 through the async proxy
+      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(v2_ready(st));
-      return true;
     };
-    uint32_t kv_it = 0, v2_it = 0;
-    int qi = 0;
-    bool ok = true;
     for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k), ++qi) {
-      int nseg = 0;
-      for (int sg = 0; sg < SEGS; ++sg) {
-        int z, h, r0;
-        nseg += decode(item, sg, z, h, r0) ? 1 : 0;
-      }
       const int qb = qi & 1;
       bool ok0 = true;
-      if (lane == 0) {
-        if ((ok0 = wait(q_empty(qb), ((qi >> 1) & 1) ^ 1, kErrQEmpty))) {
-          mbar_arrive_expect_tx(q_full(qb), nseg * C::SEG_ROWS * DQK);
-          for (int sg = 0; sg < SEGS; ++sg) {
-            int z, h, r0;
-            if (!decode(item, sg, z, h, r0)) continue;
-#pragma unroll
-            for (int at = 0; at < C::NQA; ++at)
-              tma_load_4d(sbase + C::OFF_Q + qb * C::Q_BYTES + at * kBM * C::QA + sg * C::SEG_ROWS * C::QA, &tmQ,
-                          q_full(qb), at * C::QA, r0, h, z);
-          }
-        }
-      }
+      if (lane == 0) ok0 = wait(q_full(qb), (qi >> 1) & 1, kErrQFull);
       if (!(ok = __shfl_sync(0xffffffffu, ok0, 0))) break;
-      for (int j = 0; j < nch; ++j, ++kv_it) {
-        if (C::ILV && kv_it >= LAG) {
-          if (!(ok = build_v2(v2_it))) break;
-          ++v2_it;
-        }
+      tc_fence_after();
+      const uint32_t qaddr = sbase + C::OFF_Q + qb * C::Q_BYTES;
+      for (int j = 0; j < nch; ++j, ++g) {
+        const int st = g % C::KVS;
+        // every lane that reads the chunk (V2 build) observes its arrival itself
+        if (C::ILV || lane == 0) ok0 = wait(kv_full(st), (g / C::KVS) & 1, kErrKvFull);
+        if (!(ok = __all_sync(0xffffffffu, ok0))) break;
         if (lane == 0) {
-          const int st = kv_it % C::KVS;
-          if ((ok0 = wait(kv_empty(st), ((kv_it / C::KVS) & 1) ^ 1, kErrKvEmpty))) {
-            mbar_arrive_expect_tx(kv_full(st), nseg * (C::K_SEG + C::V_SEG + C::B_BYTES / SEGS));
-            for (int sg = 0; sg < SEGS; ++sg) {
-              int z, h, r0;
-              if (!decode(item, sg, z, h, r0)) continue;
-#pragma unroll
-              for (int at = 0; at < C::NQA; ++at)
-                tma_load_4d(sbase + C::OFF_K + st * C::K_BYTES + sg * C::K_SEG + at * kBN * C::QA, &tmK,
-                            kv_full(st), at * C::QA, j * kBN, h, z);
-              tma_load_4d(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, &tmV, kv_full(st), a.v_col0,
-                          j * kBN, h, z);
-              if (BIAS)
-                tma_load_4d(sbase + C::OFF_B + st * C::B_BYTES + sg * C::SEG_ROWS * 128, &tmB, kv_full(st), j * kBN,
-                            r0, a.bias_hb ? h : 0, a.bias_zb ? (a.bias_zmod ? z % a.bias_zmod : z) : 0);
-            }
-          }
-        }
-        if (!(ok = __shfl_sync(0xffffffffu, ok0, 0))) break;
-      }
-    }
-    if (C::ILV)
-      while (ok && v2_it < kv_it) ok = build_v2(v2_it++);
-  } else if (warp == 5) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      uint32_t g = 0;
-      int qi = 0;
-      bool ok = true;
-      // acc (+)= P_gg V_gg straight into the TMEM accumulator, once the softmax
-      // warps have written P_gg and rescaled acc; `init` starts a new item
-      auto issue_pv = [&](uint32_t gg, bool init) -> bool {
-        const int slot = gg & 1;
-        const int st = gg % C::KVS;
-        if (!wait(p_full(slot), (gg >> 1) & 1, kErrPFull)) return false;
-        if (C::ILV && !wait(v2_ready(st), (gg / C::KVS) & 1, kErrV2Ready)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int sg = 0; sg < SEGS; ++sg) {
-          // the paired accumulator starts each item from the pattern the softmax
-          // warps store, so its PV MMAs always accumulate
-          const uint64_t bdesc =
-              C::ILV ? smem_desc(sbase + C::OFF_V2 + st * C::V2_BYTES + sg * C::V2_SEG, kBN * C::V2A, 8 * C::V2A,
-                                 C::SWV2)
-                     : smem_desc(sbase + C::OFF_V + st * C::V_BYTES + sg * C::V_SEG, kBN * C::VA, 8 * C::VA, C::SWV);
-          mma_i8_ts(tmem + C::ACC_OFF + sg * C::ACC_W, tmem + slot * C::S_COLS, bdesc, C::IDESC_PV,
-                    (C::ILV || !init) ? 1u : 0u);
-        }
-        tc_commit(acc_full(slot));
-        tc_commit(kv_empty(st));
-        return true;
-      };
-      for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k), ++qi) {
-        const int qb = qi & 1;
-        if (!(ok = wait(q_full(qb), (qi >> 1) & 1, kErrQFull))) break;
-        tc_fence_after();
-        const uint32_t qaddr = sbase + C::OFF_Q + qb * C::Q_BYTES;
-        for (int j = 0; j < nch; ++j, ++g) {
-          const int st = g % C::KVS;
-          if (!(ok = wait(kv_full(st), (g / C::KVS) & 1, kErrKvFull))) break;
           tc_fence_after();
           const uint32_t kaddr = sbase + C::OFF_K + st * C::K_BYTES;
 #pragma unroll
@@ -548,9 +537,14 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
           }
           tc_commit(s_full(g & 1));
           if (j == nch - 1) tc_commit(q_empty(qb));
-          if (j > 0 && !(ok = issue_pv(g - 1, j == 1))) break;
+          if (j > 0) ok0 = issue_pv(g - 1, j == 1);
         }
-        if (ok) ok = issue_pv(g - 1, nch == 1);
+        if (!(ok = __shfl_sync(0xffffffffu, ok0, 0))) break;
+        if (C::ILV) build_v2(st);
+      }
+      if (ok) {
+        if (lane == 0) ok0 = issue_pv(g - 1, nch == 1);
+        ok = __shfl_sync(0xffffffffu, ok0, 0);
       }
     }
   } else {
@@ -568,6 +562,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     const long long delta0 = (long long)rs * a.accM - (1ll << S);
     const float ident_lim = (float)(1ull << (S - 1)) * 0.999f / (float)(delta0 < 0 ? -delta0 : (delta0 ? delta0 : 1));
     const float two_mS = __int_as_float((127 - S) << 23);  // 2^-S
+    const bool nch_launch_ok = a.nch <= 500;
+    const int ident_lim_i = ident_lim >= 2.0e9f ? 0x7fffffff : (int)ident_lim;
     const float accM_ru = __ll2float_ru(a.accM < 0 ? -a.accM : a.accM);
     // paired-accumulator constants (see rescale): H, the high word of 2^(52+S);
     // 2^-S; 2^(52+S) + 2^(31+S); 2^(S-1); the range of A = alpha * acc_M for which
@@ -579,6 +575,24 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
     const bool s_pair = S >= 1 && S <= 32;
     const long long acc_a_lo = s_pair ? (S > 20 ? (1ll << (S - 20)) : 1ll) : (1ll << 62);
     const long long acc_a_hi = s_pair ? (2ll << S) - (S > 19 ? (1ll << (S - 19)) : 1ll) : 0ll;
+    const bool accM32 = a.accM >= 1 && a.accM < (1ll << 31) && s_pair;
+    const double accM_sd = (double)a.accM * two_mSd;                  // acc_M * 2^-S, exact
+    const double cK = -4503601774854144.0 * (double)a.accM;           // -(2^52 + 2^31) acc_M, exact
+    const float accM_f = (float)a.accM;
+    const int alpha_lo = accM32 ? (int)((acc_a_lo + a.accM - 1) / a.accM) : 1;
+    const int alpha_hi = accM32 ? (int)min((acc_a_hi - 1) / a.accM, (long long)0x7fffffff) : 0;
+    const bool pair_range = accM32 && alpha_hi >= alpha_lo;
+    // l takes the same one-FMA scale_release when its constants are acc's
+    const bool l_pair = !l_idiv && s_pair && a.lM == a.accM && a.ls == S;
+    // Bound on |acc| of a row for the kernels without a bias: while no P byte of
+    // the row has been negative and every alpha is in [0, rs],
+    //   |acc_j| <= 128 * (l_j + j + 1)  after chunk j.
+    // Each step: |rel(x)| <= |x| A / 2^S + 1/2 and rel(l) >= l A / 2^S - 1/2, so
+    // |acc_j| <= 128 (l_j - sum P_j) + K A / 2^S + 64.5 + |PV_j| with
+    // |PV_j| <= 128 sum P_j; with A / 2^S <= rs acc_M / 2^S <= 1 + 2^-10 the
+    // slack K grows by at most 128 per chunk for up to 500 chunks.
+    const bool lb_launch = !BIAS && !GEN && s_pair && S >= 10 && nch_launch_ok &&
+                           (long long)rs * a.accM - (1ll << S) <= (1ll << (S - 10));
     uint32_t g = 0;
     bool ok = true;
     for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k)) {
@@ -595,6 +609,11 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
       int m = kNegInf, l = 1;
       // upper bound on max |acc| of this row, kept in fp32 with round-up margins
       float abound = 0.f;
+      bool lb = lb_launch;  // the l-based bound on |acc| holds for this row
+      // that bound after chunk jj - 1 (INT_MAX when it does not hold)
+      auto acc_bound = [&](int jj) -> int {
+        return (lb && (unsigned)(l + jj) < (1u << 23)) ? (l + jj) << 7 : 0x7fffffff;
+      };
       // acc lives in TMEM (this warp's lanes, ACC_W columns); PV MMAs accumulate into it
       const uint32_t acc_base = tmem + lane_base + C::ACC_OFF + sg * C::ACC_W;
       if (C::ILV && active) {
@@ -609,7 +628,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
       }
 
       // acc = rel(acc, alpha) in place, once PV_gg (the previous chunk's) has landed
-      auto rescale = [&](uint32_t gg, int alpha, long long A) -> bool {
+      auto rescale = [&](uint32_t gg, int alpha, long long A, double Ad, double Cd, bool pair_ok) -> bool {
         if (!wait(acc_full(gg & 1), (gg >> 1) & 1, kErrPvFull)) return false;
         tc_fence_after();
         if constexpr (C::ILV) {
@@ -625,11 +644,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
           // FMA ((2^21 + 1) (2^S - A) 2^31, a 53-bit multiple of 2^31).  A = 0
           // (alpha = 0: the row max jumped far) makes every rel(x) 0: Ad = 0 and
           // Cd = 2^(52+S) + 2^(31+S) give exactly that.
-          const double Af = (double)A;
-          const bool fast = !acc_idiv && (A == 0 || (A >= acc_a_lo && A < acc_a_hi && abound * (float)Af * two_mS < 2.0e9f));
-          if (__all_sync(0xffffffffu, fast || !row_ok)) {
-            const double Ad = Af * two_mSd;
-            const double Cd = A == 0 ? acc_anchor : __fma_rn(-4503601774854144.0, Af, acc_anchor) + acc_half;
+          if (__all_sync(0xffffffffu, pair_ok || !row_ok)) {
 #pragma unroll
             for (int part = 0; part < C::ACC_W / 32; ++part) {
               int v[32];
@@ -702,6 +717,9 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
         if (!(ok = wait(s_full(slot), (g >> 1) & 1, kErrSFull))) break;
         tc_fence_after();
         int alpha = 0, m_new = m;
+        long long A = 0;
+        bool pairA = false;
+        double Ad = 0.0, Cd = 0.0;
         uint32_t pw[8];
         if (active) {
           int s[32];
@@ -794,13 +812,31 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
           }
           alpha = exp2_generic((int)((unsigned)m - (unsigned)m_new), rs, eM, exp_idiv);
           tmem_st8(tmem + lane_base + slot * C::S_COLS, pw);
+          // the fixed-point constants of this chunk's scale_release (acc and l):
+          // A = alpha * acc_M and the one-FMA form's Ad, Cd (see rescale)
+          A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
+          // A in [acc_a_lo, acc_a_hi) or 0 <=> alpha in [alpha_lo, alpha_hi] or 0 (acc_M < 2^31);
+          // Cd - 2^(S-1) = 2^(52+S) + 2^(31+S) + alpha * cK exactly, and for alpha = 0
+          // adding 2^(S-1) (half an ulp) rounds to even, back to 2^(52+S) + 2^(31+S)
+          pairA = pair_range && (alpha == 0 || (unsigned)(alpha - alpha_lo) <= (unsigned)(alpha_hi - alpha_lo));
+          const double alpha_d = (double)alpha;
+          Ad = alpha_d * accM_sd;
+          Cd = __fma_rn(alpha_d, cK, acc_anchor) + acc_half;
           // acc = rel(acc, alpha) before PV of this chunk is added (first chunk: acc
           // starts from PV alone).  Skipped when it is the identity for every row
           // of the warp: alpha == rs and |acc| * |rs * acc_M - 2^S| < 2^(S-1).
           if (j > 0) {
-            const long long A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
-            const bool ident = !acc_idiv && alpha == rs && abound < ident_lim;
-            if (!__all_sync(0xffffffffu, ident || !row_ok) && !(ok = rescale(g - 1, alpha, A))) break;
+            bool ident, pair_ok;
+            if (BIAS) {
+              ident = !acc_idiv && alpha == rs && abound < ident_lim;
+              pair_ok = !acc_idiv && pairA && abound * (float)alpha * accM_f * two_mS < 2.0e9f;
+            } else {
+              const int bnd = acc_bound(j);  // bounds acc after chunk j - 1
+              ident = !acc_idiv && alpha == rs && bnd < ident_lim_i;
+              pair_ok = !acc_idiv && pairA && bnd < (1 << 29);
+            }
+            if (!__all_sync(0xffffffffu, ident || !row_ok) && !(ok = rescale(g - 1, alpha, A, Ad, Cd, pair_ok)))
+              break;
           }
         }
         // P and acc are ready: release the MMA warp before the bookkeeping below,
@@ -816,11 +852,21 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
             ls0 = __dp4a((int)pw[2 * c], 0x01010101, ls0);
             ls1 = __dp4a((int)pw[2 * c + 1], 0x01010101, ls1);
           }
-          const int lr = l_idiv ? rel_idiv(l, alpha, rs)
-                                : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
+          int lr;
+          if (l_pair && pairA && (unsigned)(l + (1 << 29)) < (1u << 30)) {
+            // the acc constants, one FMA (|l| < 2^29 keeps |rel(l)| < 2^31)
+            const double y = __fma_rd(__hiloint2double((int)acc_hi, l ^ (int)0x80000000u), Ad, Cd);
+            lr = __double2loint(y) ^ (int)0x80000000u;
+          } else {
+            lr = l_idiv ? rel_idiv(l, alpha, rs)
+                        : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
+          }
           l = (int)((unsigned)lr + (unsigned)ls0 + (unsigned)ls1);
           m = m_new;
-          if (j > 0) {
+          const uint32_t neg = ((pw[0] | pw[1] | pw[2] | pw[3]) | (pw[4] | pw[5] | pw[6] | pw[7])) & 0x80808080u;
+          if (!BIAS) {
+            lb = lb && !neg && (j == 0 || (unsigned)alpha <= (unsigned)rs);  // chunk 0: acc is PV alone
+          } else if (j > 0) {
             // |rel(x)| <= |x| * |A| / 2^S + 1 (the idiv form: <= |x| * |alpha| / rs + 1),
             // |A| = |alpha| * acc_M taken in float with round-up; no bound when the
             // 64-bit product could wrap, or in the idiv form
@@ -830,8 +876,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
                          : __fmaf_ru(abound, aAbs * two_mS * 1.0001f, 2.f);
           }
           // |PV| <= 128 * sum|P|; sum|P| = ls0 + ls1 unless some P byte is negative
-          const uint32_t neg = ((pw[0] | pw[1] | pw[2] | pw[3]) | (pw[4] | pw[5] | pw[6] | pw[7])) & 0x80808080u;
-          abound = __fadd_ru(abound, neg ? 524288.f : (float)((ls0 + ls1) << 7));
+          if (BIAS) abound = __fadd_ru(abound, neg ? 524288.f : (float)((ls0 + ls1) << 7));
         }
       }
       if (!ok) break;
@@ -854,7 +899,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS
         // integer, and rounding toward zero cannot drop below the integer part.
         const float lf = __int2float_rn(l);
         const bool fast_ieee =
-            __all_sync(0xffffffffu, (l > 0 && l < (1 << 24) && abound < 8388607.f) || !row_ok);
+            __all_sync(0xffffffffu, (l > 0 && l < (1 << 24) && (BIAS ? abound < 8388607.f : acc_bound(nch) < 8388607)) ||
+                                        !row_ok);
         const float rcp = __frcp_ru(lf);
 #pragma unroll
         for (int part = 0; part < C::ACC_W / 32; ++part) {
@@ -1036,6 +1082,11 @@ static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const C
     if (per_sm[dev] == 0) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
         return set_err(QFLASH_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError()));
+      // the whole unified L1 as shared memory, so that the CTAs the other
+      // limits allow are resident at once (the default carveout can hold fewer)
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+          cudaSuccess)
+        return set_err(QFLASH_ERR_LAUNCH, "cudaFuncSetAttribute (carveout): %s", cudaGetErrorString(cudaGetLastError()));
       // resident CTAs per SM: registers, shared memory and TMEM columns
       cudaFuncAttributes fa;
       int regs = 255;
@@ -1043,7 +1094,7 @@ static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const C
       int smem_sm = 0;
       cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
       const int warp_regs = ((regs * 32 + 255) / 256) * 256;
-      const int by_regs = 65536 / (warp_regs * (kThreads / 32));
+      const int by_regs = 65536 / (warp_regs * (C::THREADS / 32));
       const int by_smem = smem_sm / (C::SMEM + 1024);
       const int by_tmem = 512 / C::TMEM_COLS;
       int v = by_regs < by_smem ? by_regs : by_smem;
@@ -1074,7 +1125,7 @@ static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const C
     kb.nitems = (int)items_for(rpi);
   }
   if (grid > kb.nitems) grid = kb.nitems;
-  kern<<<grid, kThreads, C::SMEM, stream>>>(mq, mk, mv, mb, kb);
+  kern<<<grid, C::THREADS, C::SMEM, stream>>>(mq, mk, mv, mb, kb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
