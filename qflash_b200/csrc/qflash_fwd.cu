@@ -226,6 +226,27 @@ __device__ void fill_out_nan(const KArgs& a) {
   }
 }
 
+// Bounded wait on an mbarrier phase: each try_wait may sleep up to kWaitHintNs
+// (waking when the phase completes), so a waiting warp takes few issue slots
+// from the others; the abort flag and the ~2 s limit are checked once per
+// sleep.  On giving up it records `code` in the error word, raises the CTA's
+// abort flag (so the other roles leave too) and returns false.  (Inline: an
+// out-of-line slow path measured 20-40 % slower, through the register
+// allocation a call imposes on every wait site.)
+__device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, unsigned code, volatile int* abort_flag) {
+  if (mbar_try_wait_hint(bar, parity, kWaitHintNs)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_hint(bar, parity, kWaitHintNs)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(&g_err, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ kernel
 // SEGS = 2 packs two heads (of N <= 64 rows each) into one 128-row tile:
 // rows [0, 64) belong to head 2*item, rows [64, 128) to head 2*item + 1.
@@ -273,7 +294,7 @@ struct Cfg {
   // registers per thread for MIN_CTAS CTAs of THREADS threads (multiple of 8);
   // the d = 64 one-head-per-tile kernels (ViT, DeiT) measured fastest at 144
   static constexpr int REGS_FIT = (65536 / (MIN_CTAS * THREADS)) / 8 * 8 > 255 ? 255 : (65536 / (MIN_CTAS * THREADS)) / 8 * 8;
-  static constexpr int MAX_REGS = (DQK == 64 && DV == 64 && SEGS == 1 && REGS_FIT > 144) ? 144 : REGS_FIT;
+  static constexpr int MAX_REGS = (!ILV && DQK == 64 && DV == 64 && SEGS == 1 && REGS_FIT > 144) ? 144 : REGS_FIT;
   static constexpr uint32_t IDESC_S = idesc_i8(kBM, kBN, false);
   static constexpr uint32_t IDESC_PV = idesc_i8(kBM, ILV ? V2A : DV, true);
   static constexpr uint32_t SWQ = QA == 32 ? kSw32 : (QA == 64 ? kSw64 : kSw128);
@@ -300,20 +321,25 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
                    const KArgs a_in) {
   using C = Cfg<DQK, DV, BIAS, SEGS>;
-  KArgs a = a_in;
+  // arguments are read in place (parameter space); the fixed-point constants
+  // may come from the device parameter block instead
+  const KArgs& a = a_in;
+  int k_rs = a.rs, k_eM = a.eM, k_rM = a.rM, k_mlim = a.m_lim;
+  long long k_lM = a.lM, k_accM = a.accM;
+  float k_os = a.o_scale;
   if (a_in.dparams) {
     const long long* dp = a_in.dparams;
     if (dp[0] != 0) {  // the constants could not be formed (reported by the parameter kernel)
       if (a_in.out) fill_out_nan<DV>(a_in);
       return;
     }
-    a.rs = (int)dp[1];
-    a.eM = (int)dp[2];
-    a.rM = (int)dp[3];
-    a.lM = dp[4];
-    a.accM = dp[5];
-    a.m_lim = (int)dp[6];
-    a.o_scale = __int_as_float((int)dp[P_OS]);
+    k_rs = (int)dp[1];
+    k_eM = (int)dp[2];
+    k_rM = (int)dp[3];
+    k_lM = dp[4];
+    k_accM = dp[5];
+    k_mlim = (int)dp[6];
+    k_os = __int_as_float((int)dp[P_OS]);
   }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -356,24 +382,8 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto fail = [&](unsigned code) {
-    atomicOr(&g_err, code);
-    *abort_flag = 1;
-  };
-  // Bounded wait: each try_wait may sleep up to kWaitHintNs (waking when the
-  // phase completes), so a waiting warp takes few issue slots from the others;
-  // the abort flag and the ~2 s limit are checked once per sleep.
-  auto wait = [&](uint32_t bar, uint32_t parity, unsigned code) -> bool {
-    if (mbar_try_wait_hint(bar, parity, kWaitHintNs)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait_hint(bar, parity, kWaitHintNs)) {
-      if (*abort_flag) return false;
-      if (clock64() - t0 > kWaitCycles) {
-        fail(code);
-        return false;
-      }
-    }
-    return true;
+  auto wait = [abort_flag](uint32_t bar, uint32_t parity, unsigned code) -> bool {
+    return bounded_wait(bar, parity, code, abort_flag);
   };
 
   const int nch = a.nch;
@@ -556,15 +566,15 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
     const bool acc_idiv = GEN && (a.flags & QFLASH_FLAG_ACC_IDIV);
     const bool div_full = !(a.flags & QFLASH_FLAG_DIV_IEEE);
 
-    const int rs = a.rs, eM = a.eM, rM = a.rM;
+    const int rs = k_rs, eM = k_eM, rM = k_rM;
     const int S = a.as;
     // rescaling by alpha == rs is the identity while |acc| * |delta0| < 2^(S-1)
-    const long long delta0 = (long long)rs * a.accM - (1ll << S);
+    const long long delta0 = (long long)rs * k_accM - (1ll << S);
     const float ident_lim = (float)(1ull << (S - 1)) * 0.999f / (float)(delta0 < 0 ? -delta0 : (delta0 ? delta0 : 1));
     const float two_mS = __int_as_float((127 - S) << 23);  // 2^-S
     const bool nch_launch_ok = a.nch <= 500;
     const int ident_lim_i = ident_lim >= 2.0e9f ? 0x7fffffff : (int)ident_lim;
-    const float accM_ru = __ll2float_ru(a.accM < 0 ? -a.accM : a.accM);
+    const float accM_ru = __ll2float_ru(k_accM < 0 ? -k_accM : k_accM);
     // paired-accumulator constants (see rescale): H, the high word of 2^(52+S);
     // 2^-S; 2^(52+S) + 2^(31+S); 2^(S-1); the range of A = alpha * acc_M for which
     // the one-FMA rescale is exact (empty unless 1 <= S <= 32)
@@ -575,15 +585,15 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
     const bool s_pair = S >= 1 && S <= 32;
     const long long acc_a_lo = s_pair ? (S > 20 ? (1ll << (S - 20)) : 1ll) : (1ll << 62);
     const long long acc_a_hi = s_pair ? (2ll << S) - (S > 19 ? (1ll << (S - 19)) : 1ll) : 0ll;
-    const bool accM32 = a.accM >= 1 && a.accM < (1ll << 31) && s_pair;
-    const double accM_sd = (double)a.accM * two_mSd;                  // acc_M * 2^-S, exact
-    const double cK = -4503601774854144.0 * (double)a.accM;           // -(2^52 + 2^31) acc_M, exact
-    const float accM_f = (float)a.accM;
-    const int alpha_lo = accM32 ? (int)((acc_a_lo + a.accM - 1) / a.accM) : 1;
-    const int alpha_hi = accM32 ? (int)min((acc_a_hi - 1) / a.accM, (long long)0x7fffffff) : 0;
+    const bool accM32 = k_accM >= 1 && k_accM < (1ll << 31) && s_pair;
+    const double accM_sd = (double)k_accM * two_mSd;                  // acc_M * 2^-S, exact
+    const double cK = -4503601774854144.0 * (double)k_accM;           // -(2^52 + 2^31) acc_M, exact
+    const float accM_f = (float)k_accM;
+    const int alpha_lo = accM32 ? (int)((acc_a_lo + k_accM - 1) / k_accM) : 1;
+    const int alpha_hi = accM32 ? (int)min((acc_a_hi - 1) / k_accM, (long long)0x7fffffff) : 0;
     const bool pair_range = accM32 && alpha_hi >= alpha_lo;
     // l takes the same one-FMA scale_release when its constants are acc's
-    const bool l_pair = !l_idiv && s_pair && a.lM == a.accM && a.ls == S;
+    const bool l_pair = !l_idiv && s_pair && k_lM == k_accM && a.ls == S;
     // Bound on |acc| of a row for the kernels without a bias: while no P byte of
     // the row has been negative and every alpha is in [0, rs],
     //   |acc_j| <= 128 * (l_j + j + 1)  after chunk j.
@@ -592,7 +602,7 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
     // |PV_j| <= 128 sum P_j; with A / 2^S <= rs acc_M / 2^S <= 1 + 2^-10 the
     // slack K grows by at most 128 per chunk for up to 500 chunks.
     const bool lb_launch = !BIAS && !GEN && s_pair && S >= 10 && nch_launch_ok &&
-                           (long long)rs * a.accM - (1ll << S) <= (1ll << (S - 10));
+                           (long long)rs * k_accM - (1ll << S) <= (1ll << (S - 10));
     uint32_t g = 0;
     bool ok = true;
     for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k)) {
@@ -749,30 +759,43 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
                                    __vimax3_s32(t3[6], t3[7], t3[8])),
                       __vimax3_s32(t3[9], t3[10], m));
           bool use_fast = MODE == kFast;
-          if (MODE == kChecked) use_fast = __all_sync(0xffffffffu, m_new < a.m_lim);
+          if (MODE == kChecked) use_fast = __all_sync(0xffffffffu, m_new < k_mlim);
           // In a ragged last chunk every padded column holds NEG_INF, so all of
           // them share one P value: groups of four columns past the last valid
           // one (whole eighths of the chunk) take it without recomputation.
           const int nq = nvalid >= kBN ? 4 : (nvalid + 7) >> 3;  // eighths-pairs with a valid column
-          if (use_fast) {
+          if (use_fast && nvalid >= kBN) {
+            // a full chunk: the 32 exp2 / requantise chains in one block
             const int cm1 = (int)((0u - (unsigned)m_new) * (unsigned)eM + 65536u);
             const int c3 = (int)((unsigned)rs - (unsigned)m_new);
 #pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int e0 = exp2_fast(s[4 * c + 0], eM, cm1, rs, c3);
+              const int e1 = exp2_fast(s[4 * c + 1], eM, cm1, rs, c3);
+              const int e2 = exp2_fast(s[4 * c + 2], eM, cm1, rs, c3);
+              const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
+              pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+            }
+          } else if (use_fast) {
+            // ragged last chunk (static indices throughout: pw stays in registers)
+            const int cm1 = (int)((0u - (unsigned)m_new) * (unsigned)eM + 65536u);
+            const int c3 = (int)((unsigned)rs - (unsigned)m_new);
+            const int ep = exp2_fast(kNegInf, eM, cm1, rs, c3);
+            const uint32_t pp = requant_pack4(ep, ep, ep, ep, rM);
+#pragma unroll
             for (int qd = 0; qd < 4; ++qd) {
-              if (qd > 0 && qd >= nq) {
-                const int ep = exp2_fast(kNegInf, eM, cm1, rs, c3);
-                const uint32_t pp = requant_pack4(ep, ep, ep, ep, rM);
+              if (qd == 0 || qd < nq) {
 #pragma unroll
-                for (int c = 2 * qd; c < 8; ++c) pw[c] = pp;
-                break;
-              }
-#pragma unroll
-              for (int c = 2 * qd; c < 2 * qd + 2; ++c) {
-                const int e0 = exp2_fast(s[4 * c + 0], eM, cm1, rs, c3);
-                const int e1 = exp2_fast(s[4 * c + 1], eM, cm1, rs, c3);
-                const int e2 = exp2_fast(s[4 * c + 2], eM, cm1, rs, c3);
-                const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
-                pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+                for (int c = 2 * qd; c < 2 * qd + 2; ++c) {
+                  const int e0 = exp2_fast(s[4 * c + 0], eM, cm1, rs, c3);
+                  const int e1 = exp2_fast(s[4 * c + 1], eM, cm1, rs, c3);
+                  const int e2 = exp2_fast(s[4 * c + 2], eM, cm1, rs, c3);
+                  const int e3 = exp2_fast(s[4 * c + 3], eM, cm1, rs, c3);
+                  pw[c] = requant_pack4(e0, e1, e2, e3, rM);
+                }
+              } else {
+                pw[2 * qd] = pp;
+                pw[2 * qd + 1] = pp;
               }
             }
           } else if (MODE == kChecked) {
@@ -791,14 +814,14 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
               pw[7] = w;
             }
           } else if (MODE != kFast) {
+            const int ep = exp2_generic((int)((unsigned)kNegInf - (unsigned)m_new), rs, eM, exp_idiv);
+            const uint32_t pp = requant_pack4(ep, ep, ep, ep, rM);
 #pragma unroll
             for (int qd = 0; qd < 4; ++qd) {
               if (qd > 0 && qd >= nq) {
-                const int ep = exp2_generic((int)((unsigned)kNegInf - (unsigned)m_new), rs, eM, exp_idiv);
-                const uint32_t pp = requant_pack4(ep, ep, ep, ep, rM);
-#pragma unroll
-                for (int c = 2 * qd; c < 8; ++c) pw[c] = pp;
-                break;
+                pw[2 * qd] = pp;
+                pw[2 * qd + 1] = pp;
+                continue;
               }
 #pragma unroll
               for (int c = 2 * qd; c < 2 * qd + 2; ++c) {
@@ -814,7 +837,7 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
           tmem_st8(tmem + lane_base + slot * C::S_COLS, pw);
           // the fixed-point constants of this chunk's scale_release (acc and l):
           // A = alpha * acc_M and the one-FMA form's Ad, Cd (see rescale)
-          A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)a.accM);
+          A = (long long)((unsigned long long)(long long)alpha * (unsigned long long)k_accM);
           // A in [acc_a_lo, acc_a_hi) or 0 <=> alpha in [alpha_lo, alpha_hi] or 0 (acc_M < 2^31);
           // Cd - 2^(S-1) = 2^(52+S) + 2^(31+S) + alpha * cK exactly, and for alpha = 0
           // adding 2^(S-1) (half an ulp) rounds to even, back to 2^(52+S) + 2^(31+S)
@@ -859,7 +882,7 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
             lr = __double2loint(y) ^ (int)0x80000000u;
           } else {
             lr = l_idiv ? rel_idiv(l, alpha, rs)
-                        : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)a.lM, a.ls);
+                        : rel_shift64(l, (unsigned long long)(long long)alpha * (unsigned long long)k_lM, a.ls);
           }
           l = (int)((unsigned)lr + (unsigned)ls0 + (unsigned)ls1);
           m = m_new;
@@ -948,7 +971,7 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
             uint8_t* drow = (uint8_t*)a.out +
                             ((long long)z * a.ou_z + (long long)h * a.ou_h + (long long)row * a.ou_n + a.v_col0 +
                              part * EPP) * esz;
-            store_dequant<EPP>(drow, res, a.o_scale, a.out_dtype, a.out_vec16);
+            store_dequant<EPP>(drow, res, k_os, a.out_dtype, a.out_vec16);
           } else if (row_ok) {
             if (a.o_vec16) {
 #pragma unroll

@@ -252,6 +252,45 @@ __device__ __forceinline__ void tmem_st64(uint32_t taddr, const int (&v)[64]) {
       "r"(v[63])
       : "memory");
 }
+// 16-lane accesses (.16x32bx2): the warp reads or writes 16 TMEM lanes starting
+// at the lane of taddr; thread t < 16 takes lane base + t at columns
+// [c, c + n), thread t + 16 the same lane at columns [c + OFF, c + OFF + n).
+// Two threads thus share one row, each with its own half of the columns.
+template <int OFF>
+__device__ __forceinline__ void tmem_ld16x2_16(uint32_t taddr, int (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16], %17;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr), "n"(OFF)
+      : "memory");
+}
+template <int OFF>
+__device__ __forceinline__ void tmem_ld16x2_32(uint32_t taddr, int (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], %33;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr), "n"(OFF)
+      : "memory");
+}
+// 4 columns per thread into TMEM (16-lane shape), then wait for the store.
+template <int OFF>
+__device__ __forceinline__ void tmem_st16x2_4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x4.b32 [%0], %5, {%1,%2,%3,%4};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "n"(OFF)
+      : "memory");
+}
+// 32 columns per thread into TMEM (16-lane shape); awaited with tmem_wait_st.
+template <int OFF>
+__device__ __forceinline__ void tmem_st16x2_32(uint32_t taddr, const int (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x32.b32 [%0], %33, {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]), "n"(OFF)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- descriptors
