@@ -189,6 +189,18 @@ int qflash_device_error(void* stream, uint32_t* out);
  * current device.  No counterpart in the reference. */
 int qflash_selftest_wait_timeout(void* stream, long long max_cycles);
 
+/* Measured dense int8 tensor-core throughput, the denominator of the benchmark's
+ * tensor roofline: ctas_per_sm (1 or 2) CTAs per SM each issue `iters`
+ * back-to-back tcgen05.mma kind::i8 of M = 128, N = 256, K = 32 (2 * 128 * 256 *
+ * 32 integer ops each) from shared memory into TMEM and wait for them.  The
+ * caller times the launch on `stream` (CUDA events) and divides
+ * SMs * ctas_per_sm * iters * 2097152 ops by the elapsed time.  No counterpart
+ * in the reference (its contractions are the Triton tl.dot calls at
+ * qflash/kernel.py:153,171). */
+int qflash_i8_mma_peak(int ctas_per_sm, int iters, void* stream);
+/* Synchronises the stream; *out = 1 if a peak-kernel wait gave up, else 0 (read and clear). */
+int qflash_i8_mma_peak_status(void* stream, uint32_t* out);
+
 /* Number of kernel launches issued by this library since load (for accounting). */
 uint64_t qflash_launch_count(void);
 

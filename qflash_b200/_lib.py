@@ -69,6 +69,8 @@ SIGNATURES = {
     "qflash_version": (ctypes.c_char_p, []),
     "qflash_last_error": (ctypes.c_char_p, []),
     "qflash_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
+    "qflash_i8_mma_peak": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "qflash_i8_mma_peak_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 _lock = threading.Lock()
@@ -194,3 +196,26 @@ def launch_count() -> int:
 
 def last_grid() -> int:
     return int(load().qflash_last_grid())
+
+
+def i8_mma_peak_tops(ctas_per_sm: int = 1, iters: int = 20000, reps: int = 5) -> float:
+    """Measured dense int8 tensor-core throughput of the current GPU in TOPS
+    (best of `reps` timed launches of qflash_i8_mma_peak, CUDA events)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    _check(load().qflash_i8_mma_peak(ctas_per_sm, iters, stream.cuda_stream), "qflash_i8_mma_peak")  # warm-up
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _check(load().qflash_i8_mma_peak(ctas_per_sm, iters, stream.cuda_stream), "qflash_i8_mma_peak")
+        e1.record(stream)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    err = ctypes.c_uint32(0)
+    _check(load().qflash_i8_mma_peak_status(stream.cuda_stream, ctypes.byref(err)), "qflash_i8_mma_peak_status")
+    if err.value:
+        raise QFlashError("the int8 MMA peak kernel's wait gave up")
+    ops = sms * ctas_per_sm * iters * 2.0 * 128 * 256 * 32
+    return ops / (best * 1e-3) / 1e12

@@ -629,7 +629,13 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
       if (C::ILV && active) {
         // paired accumulator: every item starts from acc = 0, i.e. (2^31, H) pairs;
         // the stores complete (tcgen05.wait::st of the P store) before this
-        // warp releases the item's first P to the MMA warp
+        // warp releases the item's first P to the MMA warp.  The PV MMAs write
+        // all 128 lanes, so the previous item's last PV must have landed first:
+        // a warp with no rows in that item (past N) never waited for it.
+        if (g > 0) {
+          if (!(ok = wait(acc_full((g - 1) & 1), ((g - 1) >> 1) & 1, kErrPvFull))) break;
+          tc_fence_after();
+        }
         int pat[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) pat[i] = (i & 1) ? (int)acc_hi : (int)0x80000000u;

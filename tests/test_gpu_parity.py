@@ -191,3 +191,39 @@ def test_many_heads_of_few_chunks(N, D):
         ref = orc.attention_int8(q8[z:z + 1, h:h + 1].numpy(), k8[z:z + 1, h:h + 1].numpy(),
                                  v8[z:z + 1, h:h + 1].numpy(), prm)
         assert np.array_equal(ref[0, 0], got[z, h]), f"head ({z}, {h}) differs"
+
+
+def _oracle_head(args):
+    q, k, v, prm = args
+    return orc.attention_int8(q, k, v, prm)[0, 0]
+
+
+def test_full_vit_b_workload_every_head():
+    """The whole ViT-B attention layer (3072 heads, many work items per CTA, the
+    second 128-row tile of each head partly past N) against the oracle on every
+    head (IEEE division, as the oracle computes): catches anything that depends
+    on the order of items within a CTA (e.g. TMEM reuse between items)."""
+    import multiprocessing as mp
+    import os
+    from qflash_b200 import _lib
+    from qflash_b200 import kernel as K
+    from qflash_b200.workloads import WORKLOADS, make_inputs
+    w = WORKLOADS["vit_b"]
+    q, k, v, _ = make_inputs(w, seed=11, device="cuda")
+    qs, ks, vs = (t.abs().amax() / 127 for t in (q, k, v))
+    sm, rs, eM, rM, lM, aM = K.fixed_point_params(float((qs * ks).item()), w.D, None)
+    q8, k8, v8 = K.quantize(q, qs), K.quantize(k, ks), K.quantize(v, vs)
+    o8 = torch.empty_like(v8)
+    for _ in range(3):   # repeated launches: timing-dependent faults get several chances
+        K.launch_int8(q8, k8, v8, o8, rs, eM, rM, lM, aM, flags=K.arith_flags(div_mode="ieee"))
+        torch.cuda.synchronize()
+        assert _lib.device_error(torch.cuda.current_stream().cuda_stream) == 0
+        got = o8.cpu().numpy()
+        prm = orc.Params(sm, rs, eM, rM, lM, aM)
+        q8n, k8n, v8n = (t.cpu().numpy() for t in (q8, k8, v8))
+        tasks = [(q8n[z:z + 1, h:h + 1], k8n[z:z + 1, h:h + 1], v8n[z:z + 1, h:h + 1], prm)
+                 for z in range(w.Z) for h in range(w.H)]
+        with mp.get_context("spawn").Pool(max(1, min(32, os.cpu_count() or 1))) as pool:
+            refs = pool.map(_oracle_head, tasks, chunksize=64)
+        bad = [(i // w.H, i % w.H) for i, r in enumerate(refs) if not np.array_equal(r, got[i // w.H, i % w.H])]
+        assert not bad, f"{len(bad)} heads differ, e.g. {bad[:5]}"
