@@ -57,6 +57,8 @@ extern "C" {
  *   flags           QFLASH_FLAG_*
  *   stream          cudaStream_t (NULL = legacy default stream)
  * Pointers and the q/k/v/bias strides of the three outer dimensions must be 16-byte aligned.
+ * Every entry point makes the device that owns q current for its launches and
+ * restores the calling thread's current device before it returns.
  */
 int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
                   const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
@@ -163,9 +165,9 @@ int qflash_fused_status(const void* workspace, void* stream, int64_t* status);
  * the library (every GPU that loads the library holds it until exit), enough
  * for the constants plus an int32 bias of a mask up to about 4 MiB at
  * [mask_zb, mask_hb, N, N rounded up to 4] int32; larger masks are rejected
- * with QFLASH_ERR_UNSUPPORTED.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  Every call shares the one array: calls whose
+ * with QFLASH_ERR_UNSUPPORTED.  The array's device address is looked up
+ * (cudaGetSymbolAddress) on every call made outside a stream capture, so a
+ * device's first call must come before any capture.  Every call shares the one array: calls whose
  * work overlaps on the GPU (other streams, other threads) race and corrupt
  * each other; serialise them.  Nothing in the array needs to start at zero --
  * each call writes every byte it later reads -- so stale contents from an
@@ -177,6 +179,16 @@ int qflash_fwd_fused_noalloc(const void* q, const void* k, const void* v, int dt
                              int mask_z_period, int8_t* q8, int8_t* k8, int8_t* v8, int8_t* o8, void* out, int Z,
                              int H, int N, int D, double scale_log2e, int32_t l_shift, int32_t acc_shift,
                              uint32_t flags, void* stream);
+
+/*
+ * Status of the last qflash_fwd_fused_noalloc call on the device that owns q
+ * (the same codes as qflash_fused_status; no counterpart in the reference):
+ * the no-alloc caller has no workspace pointer to hand qflash_fused_status, so
+ * this reads the library's scratch array of that device.  Synchronises the
+ * stream.  The scratch keeps the most recent call's status, whichever stream
+ * made it.
+ */
+int qflash_fused_noalloc_status(const void* q, void* stream, int64_t* status);
 
 /* Reads and clears the device-side error word the kernels set when a bounded
  * wait gives up (0 = none).  Synchronises the stream. */

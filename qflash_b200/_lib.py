@@ -70,6 +70,7 @@ SIGNATURES = {
     "qflash_last_error": (ctypes.c_char_p, []),
     "qflash_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
     "qflash_i8_mma_peak": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "qflash_fused_noalloc_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)]),
     "qflash_i8_mma_peak_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
 }
 

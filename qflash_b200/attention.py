@@ -1,5 +1,5 @@
 """QAttention / QWindowAttention / patch_attention: the reference's model
-integration (qflash/attention.py:16-112) over this package's qflash.forward.
+integration (qflash/attention.py:12-108) over this package's qflash.forward.
 
 timm is optional: its helpers are replaced by local equivalents when it is not
 installed; ``patch_attention`` needs timm (it swaps timm modules).
@@ -30,7 +30,7 @@ except ImportError:
 
 
 class QAttention(nn.Module):
-    """qflash/attention.py:16-40."""
+    """qflash/attention.py:12-36."""
 
     def __init__(self, dim: int, num_heads: int, qkv_bias: bool = True):
         super().__init__()
@@ -48,7 +48,8 @@ class QAttention(nn.Module):
             # the attention epilogue writes [B, N, H, D] directly: the reshape
             # below is then a view instead of a transpose copy
             out = torch.empty((B, N, self.num_heads, self.head_dim), dtype=q.dtype, device=x.device)
-            K.forward_fused(q, k, v, out=out.permute(0, 2, 1, 3))
+            # check: raise where the reference's qflash.forward raises (an all-zero q or k)
+            K.forward_fused(q, k, v, out=out.permute(0, 2, 1, 3), check=True)
             return self.proj(out.reshape(B, N, C))
         x = qflash.forward(q, k, v, attn_mask=attn_mask)
         return self.proj(x.transpose(1, 2).reshape(B, N, C))
@@ -65,7 +66,7 @@ class QAttention(nn.Module):
 
 
 class QWindowAttention(nn.Module):
-    """qflash/attention.py:43-90."""
+    """qflash/attention.py:39-86."""
 
     def __init__(self, dim: int, num_heads: int, window_size, qkv_bias: bool = True):
         super().__init__()
@@ -121,24 +122,26 @@ class QWindowAttention(nn.Module):
 
 
 def patch_attention(model: nn.Module) -> Dict[str, int]:
-    """Swap timm Attention / WindowAttention modules in place
-    (qflash/attention.py:93-112).  Needs timm."""
-    import timm.layers.attention as _ta
-    import timm.models.swin_transformer as _ts
+    """Replace every timm ``Attention`` / ``WindowAttention`` submodule of
+    ``model`` by QAttention / QWindowAttention carrying the same weights
+    (qflash/attention.py:89-108); returns how many of each were replaced.
+    Needs timm."""
+    import timm.layers.attention as timm_attention
+    import timm.models.swin_transformer as timm_swin
 
-    targets = []
+    replacement = ((timm_attention.Attention, QAttention, "attn"),
+                   (timm_swin.WindowAttention, QWindowAttention, "wattn"))
+    # decide on the original tree first, then swap (named_modules would walk the new modules)
+    plan = []
     for name, module in model.named_modules():
-        if isinstance(module, _ta.Attention):
-            targets.append((name, "attn"))
-        elif isinstance(module, _ts.WindowAttention):
-            targets.append((name, "wattn"))
-
+        for timm_cls, q_cls, key in replacement:
+            if isinstance(module, timm_cls):
+                plan.append((name, q_cls, key))
+                break
     counts = {"attn": 0, "wattn": 0}
-    for name, kind in targets:
-        parent_name, _, child_name = name.rpartition(".")
-        parent = model.get_submodule(parent_name) if parent_name else model
-        src = getattr(parent, child_name)
-        new = (QAttention if kind == "attn" else QWindowAttention).from_orig(src)
-        setattr(parent, child_name, new)
-        counts[kind] += 1
+    for name, q_cls, key in plan:
+        owner_name, _, attr = name.rpartition(".")
+        owner = model.get_submodule(owner_name) if owner_name else model
+        setattr(owner, attr, q_cls.from_orig(getattr(owner, attr)))
+        counts[key] += 1
     return counts

@@ -1,5 +1,7 @@
 // Declarations shared by the library's translation units (not part of the C ABI).
 #pragma once
+#include <cuda_runtime.h>
+
 #include <cstddef>
 #include <cstdint>
 
@@ -37,6 +39,24 @@ struct WindowBiasSpec {
 };
 
 int set_err(int code, const char* fmt, ...);
+
+// Restores the calling thread's current device when it goes out of scope: the
+// entry points make the device that owns the data current for their launches
+// and leave the caller's choice as they found it.
+struct DeviceGuard {
+  int prev = -1;
+  DeviceGuard() {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      cudaGetLastError();
+      prev = -1;
+    }
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
 int select_device(const void* p, int* dev);
 int sm_count(int dev);
 

@@ -1221,6 +1221,7 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
   if (flags & ~(QFLASH_FLAG_EXP_IDIV | QFLASH_FLAG_L_IDIV | QFLASH_FLAG_ACC_IDIV | QFLASH_FLAG_DIV_FULL |
                 QFLASH_FLAG_DIV_IEEE))
     return set_err(QFLASH_ERR_ARG, "unknown flag bits 0x%x", flags);
+  DeviceGuard keep_device;  // the caller's current device is restored on return
   int dev = 0;
   if (int rc0 = select_device(q, &dev)) return rc0;
 

@@ -538,6 +538,7 @@ int fused_fwd(const void* q, const void* k, const void* v, int dtype, const int6
   const size_t need = fused_workspace_bytes(has_mask ? mask_zb : 0, has_mask ? mask_hb : 0, N);
   if (ws_bytes < need) return set_err(QFLASH_ERR_ARG, "workspace of %zu bytes, %zu needed", ws_bytes, need);
   if ((uintptr_t)ws & 255) return set_err(QFLASH_ERR_ALIGN, "workspace must be 256-byte aligned");
+  DeviceGuard keep_device;  // the caller's current device is restored on return
   int dev = 0;
   if (int rc0 = select_device(q, &dev)) return rc0;
 

@@ -344,7 +344,7 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
 
 
 def forward_window_fused(query, key, value, table, index, window_mask=None, scale=None, check=True, out=None):
-    """QWindowAttention's attention (qflash/attention.py:64-76) with every step
+    """QWindowAttention's attention (qflash/attention.py:63-75) with every step
     on the device, the bias included (qflash_fwd_fused_window): the float mask
     entry (b, h, i, j) is table[index[i, j], h] + window_mask[b % nW, i, j],
     formed and quantised once per window and head.  Same bits as
@@ -396,7 +396,7 @@ def window_attention(query, key, value, rel_bias, window_mask=None, scale=None, 
 
     Equals ``qflash_forward(query, key, value, attn_mask=rel_bias + mask)``
     with the [B_, H, N, N] float mask that QWindowAttention builds
-    (qflash/attention.py:72-76) -- bit for bit, because that mask's entry
+    (qflash/attention.py:68-74) -- bit for bit, because that mask's entry
     (b, h) is rel_bias[h] + window_mask[b % nW] and the bias quantisation is
     elementwise.  Here the sum and its quantisation are formed once per
     (window, head), [nW, H, N, N], and the kernel reads entry b % nW, so

@@ -1,6 +1,6 @@
 """Swin window-attention helpers, written from their definitions.
 
-``QWindowAttention`` (qflash/attention.py:43-79) takes its relative-position
+``QWindowAttention`` (qflash/attention.py:39-86) takes its relative-position
 index from timm (``get_relative_position_index``) and receives timm's
 shifted-window mask.  timm is optional here, so both are defined below from
 the Swin Transformer construction they follow.
@@ -51,7 +51,7 @@ def shifted_window_mask(img_h: int, img_w: int, window: int, shift: int,
 
 def window_bias(table: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
     """Relative-position bias [1, H, N, N] gathered from ``table`` [T, H]
-    (qflash/attention.py:62-65)."""
+    (qflash/attention.py:58-61)."""
     n = index.shape[0]
     b = table[index.reshape(-1)].view(n, n, -1).permute(2, 0, 1).contiguous()
     return b.unsqueeze(0)
@@ -60,7 +60,7 @@ def window_bias(table: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
 def window_attn_mask(table: torch.Tensor, index: torch.Tensor, num_images: int,
                      mask: torch.Tensor | None) -> torch.Tensor:
     """The float ``attn_mask`` that QWindowAttention.forward hands to
-    ``qflash.forward`` (qflash/attention.py:72-76): bias + the window mask
+    ``qflash.forward`` (qflash/attention.py:68-74): bias + the window mask
     broadcast over images and heads, shape [B_, H, N, N] (or [1, H, N, N]
     without a mask)."""
     attn_mask = window_bias(table, index)

@@ -43,7 +43,7 @@ class Workload:
         return Workload(self.name, Z, self.H, self.N, self.D, self.dist)
 
 
-# cfg1 (CPU case), cfg2 (headline), cfg3, cfg4 (two Swin stages), cfg5.
+# ViT-S (the CPU case), ViT-B/16 (headline), DeiT-T, Swin-T stages 1 and 4, ViT-L/16 @384.
 WORKLOADS = {
     "vit_s": Workload("vit_s", 8, 6, 197, 64, "normal"),
     "vit_b": Workload("vit_b", 256, 12, 197, 64, "head_std"),

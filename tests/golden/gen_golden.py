@@ -133,7 +133,7 @@ def swin_mask(seed, images, heads, windows):
 def cases():
     """(name, env, builder) -- builder returns (q, k, v, attn_mask, scale)."""
     D = {}
-    # BASELINE configs at reduced batch (same N, d, H-distribution)
+    # the ViT-S/B/L, DeiT-T and Swin-T workloads at reduced batch (same N, d, H-distribution)
     D["cfg1_vit_s"] = ({}, lambda: (*gen(1, (1, 3, 197, 64)), None, None))
     D["cfg2_vit_b"] = ({}, lambda: (*gen(2, (1, 4, 197, 64), "head_std"), None, None))
     D["cfg3_deit_t"] = ({}, lambda: (*gen(3, (1, 3, 197, 64), "outlier"), None, None))

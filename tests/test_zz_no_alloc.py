@@ -101,3 +101,40 @@ def test_noalloc_rejects_a_mask_beyond_the_scratch():
     rc = _lib.load().qflash_fwd_fused_noalloc(*head, torch.cuda.current_stream().cuda_stream)
     assert rc == -6  # QFLASH_ERR_UNSUPPORTED
     assert b"scratch" in _lib.load().qflash_last_error()
+
+
+def test_noalloc_status_reader_and_argument_checks():
+    """The no-alloc caller reads the status of its last call through
+    qflash_fused_noalloc_status (an all-zero q: status 1, where the reference
+    raises ZeroDivisionError); bad mask extents are argument errors."""
+    q, k, v = (torch.randn(2, 3, 40, 32, device="cuda") for _ in range(3))
+    q.zero_()
+    head, _bufs = _args(q, k, v, None, 0)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert _lib.load().qflash_fwd_fused_noalloc(*head, stream) == 0
+    st = ctypes.c_int64(-7)
+    assert _lib.load().qflash_fused_noalloc_status(q.data_ptr(), stream, ctypes.byref(st)) == 0
+    assert st.value == 1
+    q2 = torch.randn_like(k)
+    head, _bufs = _args(q2, k, v, None, 0)
+    assert _lib.load().qflash_fwd_fused_noalloc(*head, stream) == 0
+    assert _lib.load().qflash_fused_noalloc_status(q2.data_ptr(), stream, ctypes.byref(st)) == 0
+    assert st.value == 0
+    m = torch.zeros(2, 3, 40, 40, device="cuda")
+    head, _bufs = _args(q2, k, v, m, 0)
+    head = list(head)
+    head[10] = -1        # mask_zb
+    assert _lib.load().qflash_fwd_fused_noalloc(*head, stream) == -1   # QFLASH_ERR_ARG
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_entry_points_restore_the_current_device():
+    """A call with data on device 1 while device 0 is current leaves device 0 current."""
+    torch.cuda.set_device(0)
+    x = torch.randn(1, 2, 64, 32, device="cuda:1")
+    head, _bufs = _args(x, x, x, None, 0)
+    with torch.cuda.device(1):
+        stream = torch.cuda.current_stream().cuda_stream
+    assert _lib.load().qflash_fwd_fused_noalloc(*head, stream) == 0
+    torch.cuda.synchronize(1)
+    assert torch.cuda.current_device() == 0
