@@ -181,12 +181,16 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline and parity sample (profiling runs)")
     ap.add_argument("--no-triton", action="store_true", help="skip the reference Triton kernel on the GPU")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the workload's batch Z (smaller cases for profiler captures; not a bench line)")
     a = ap.parse_args()
     if a.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
 
     from qflash_b200.workloads import WORKLOADS
     w = WORKLOADS[a.workload]
+    if a.batch:
+        w = w.scaled(a.batch)
     metric = f"int8 attn TOPS & us/call ({w.name} Z={w.Z} H={w.H} N={w.N} d={w.D}) and % of int8 TC/HBM roofline"
     rank, world, local = dist_setup(a.gpus)
 

@@ -263,7 +263,9 @@ struct Cfg {
   // column pair reads as the double 2^(52+S) + (acc + 2^31) * 2^S and the
   // fixed-point rescale is one FMA per element.  The PV MMA then multiplies by
   // V2, V with a zero byte after every element (built in shared memory).
-  static constexpr bool ILV = 2 * S_COLS + SEGS * 2 * DV <= 256;
+  // (one head per tile only: with two heads of at most two chunks per tile
+  // (Swin windows) an item rescales once, and the plain layout measured faster)
+  static constexpr bool ILV = SEGS == 1 && 2 * S_COLS + 2 * DV <= 256;
   static constexpr int ACC_W = ILV ? 2 * DV : DV;   // TMEM columns of acc per segment
   static constexpr int V2A = 2 * DV;                // bytes per key row of V2 (one swizzle atom)
   static constexpr int KVS = BIAS ? 4 : 8;          // K/V chunk stages
