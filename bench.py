@@ -128,9 +128,10 @@ def _oracle_worker(args):
     return orc.attention_int8(q, k, v, prm, b)
 
 
-def run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs, bias=None):
-    """Time the oracle on the sampled heads with ``procs`` worker processes
-    (spawned; each head is an independent task)."""
+def run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs, bias=None, passes=1):
+    """Time ``passes`` runs of the oracle over the sampled heads with ``procs``
+    worker processes (spawned; each head is an independent task); the outputs
+    are those of the first pass."""
     from oracle import qflash_oracle as orc
     tasks = [(q8n[z:z + 1, h:h + 1], k8n[z:z + 1, h:h + 1], v8n[z:z + 1, h:h + 1], prm,
               None if bias is None else bias[z:z + 1, h:h + 1]) for z, h in zip(zs, hs)]
@@ -144,6 +145,8 @@ def run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs, bias=None):
         pool.map(_oracle_worker, tasks[:procs])           # warm the workers
         t0 = time.perf_counter()
         outs = pool.map(_oracle_worker, tasks, chunksize=max(1, len(tasks) // (4 * procs)))
+        for _ in range(passes - 1):
+            pool.map(_oracle_worker, tasks, chunksize=max(1, len(tasks) // (4 * procs)))
         dt = time.perf_counter() - t0
     return dt, outs
 
@@ -241,6 +244,16 @@ def main():
         sets.append((q8.clone(), k8.clone(), v8.clone(), torch.empty_like(v8)))
     gathered = torch.empty((world * zmax, w.H, w.N, w.D), dtype=torch.int8, device=dev) if world > 1 else None
     o_pad = torch.zeros((zmax, w.H, w.N, w.D), dtype=torch.int8, device=dev) if world > 1 and zl != zmax else None
+    peer = None
+    amax3 = None
+    if world > 1:
+        from qflash_b200.shard import PeerOutput
+        # the gathered int8 O on every rank, filled by every rank's attention epilogue
+        peer = PeerOutput((w.Z, w.H, w.N, w.D))
+        peer_dst, peer_rows = peer.buffer[z0:z1], peer.peer_rows(z0)
+        # this rank's |max| of its float Q/K/V shards: the global-scale reduction of forward_sharded
+        amax3 = torch.stack([t[z0:z1].abs().amax().float() for t in (q, k, v)])
+        sync1 = torch.zeros(1, device=dev)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
@@ -248,6 +261,17 @@ def main():
     def kernel(i):
         s = sets[i % n_sets]
         K.launch_int8(s[0], s[1], s[2], s[3], rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period)
+
+    def kernel_gather(i):
+        # the attention kernel storing its rows into every rank's gathered copy
+        s = sets[i % n_sets]
+        K.launch_int8(s[0], s[1], s[2], peer_dst, rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period,
+                      o_peers=peer_rows)
+
+    def order():
+        # every rank's kernel precedes its part of this collective: afterwards
+        # all peer stores into this rank's copy are done
+        dist.all_reduce(sync1)
 
     def gather(i):
         o = sets[i % n_sets][3]
@@ -257,9 +281,18 @@ def main():
         dist.all_gather_into_tensor(gathered, o)
 
     def step(i):
-        kernel(i)
         if world > 1:
-            gather(i)
+            dist.all_reduce(amax3, op=dist.ReduceOp.MAX)   # global scales (3 scalars)
+            kernel_gather(i)
+            order()
+        else:
+            kernel(i)
+
+    def step_nccl(i):
+        # the same step with the result collective as a separate NCCL all_gather
+        dist.all_reduce(amax3, op=dist.ReduceOp.MAX)
+        kernel(i)
+        gather(i)
 
     def timed(fn, n):
         """ms per call of fn over n calls: CUDA events on the launching stream, max over ranks."""
@@ -303,24 +336,42 @@ def main():
         ms_total = float(t.item())
     ms_step = ms_total / a.steps
     assert _lib.device_error(sp) == 0
-    kernel_ms = timed(kernel, min(a.steps, 200)) if world > 1 else ms_step
-    gather_ms = timed(gather, min(a.steps, 50)) if world > 1 else 0.0
+    kernel_ms = timed(kernel_gather, min(a.steps, 200)) if world > 1 else ms_step
+    multi = None
+    if world > 1:
+        multi = {"kernel_ms": round(kernel_ms, 4),
+                 "kernel_local_only_ms": round(timed(kernel, min(a.steps, 200)), 4),
+                 "order_allreduce_ms": round(timed(lambda i: order(), min(a.steps, 200)), 4),
+                 "scale_allreduce_ms": round(timed(lambda i: dist.all_reduce(amax3, op=dist.ReduceOp.MAX),
+                                                   min(a.steps, 200)), 4),
+                 "step_ms": round(ms_step, 4),
+                 "nccl_gather_ms": round(timed(gather, min(a.steps, 50)), 4),
+                 "nccl_step_ms": round(timed(step_nccl, min(a.steps, 100)), 4),
+                 "collective": "the attention epilogue stores every O row into every rank's copy of the gathered "
+                               "output (CUDA IPC mappings, P2P stores over NVLink), then a 1-element NCCL "
+                               "all_reduce orders those stores; nccl_step_ms: the same step with NCCL "
+                               "all_gather_into_tensor after a local-only kernel"}
 
-    # the gathered output equals the single-GPU output bit for bit (rank 0 computes it)
+    # the gathered output (both collectives) equals the single-GPU output bit for bit
     multi_exact = None
     if world > 1:
+        peer.buffer.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        step(0)
+        kernel(0)
         gather(0)
         torch.cuda.synchronize()
-        if rank == 0:
-            o_full = torch.empty_like(v8f)
-            K.launch_int8(q8f, k8f, v8f, o_full, rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period)
-            torch.cuda.synchronize()
-            got = torch.cat([gathered[r * zmax: r * zmax + (shard_bounds(w.Z, world, r)[1] - shard_bounds(w.Z, world, r)[0])]
-                             for r in range(world)])
-            multi_exact = bool(torch.equal(got, o_full))
-            del o_full, got
-        t = torch.tensor([1 if (multi_exact is None or multi_exact) else 0], device=dev)
-        dist.broadcast(t, 0)
+        o_full = torch.empty_like(v8f)
+        K.launch_int8(q8f, k8f, v8f, o_full, rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period)
+        torch.cuda.synchronize()
+        got = torch.cat([gathered[r * zmax: r * zmax + (shard_bounds(w.Z, world, r)[1] - shard_bounds(w.Z, world, r)[0])]
+                         for r in range(world)])
+        ok = torch.tensor([int(torch.equal(peer.buffer, o_full) and torch.equal(got, o_full))], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)   # every rank's copy
+        multi_exact = bool(ok.item())
+        multi["gathered_bit_exact_vs_1gpu"] = multi_exact
+        del o_full, got
 
     # End to end through the public API: every step copies this rank's fp16 Q/K/V
     # from pinned host memory, runs qflash.forward (the drop-in entry point: the
@@ -456,22 +507,22 @@ def main():
     # kernel timed the same way on the same int8 tensors, and the public outputs
     # compared bit for bit on the whole workload.
     triton_ref = None
-    if world == 1 and not a.no_triton and win is None:
+    if world == 1 and not a.no_triton:
         try:
             ref, why = load_reference_kernel()
             if ref is None:
                 triton_ref = {"unavailable": why}
             else:
                 t0 = time.perf_counter()
-                ref_out = ref.qflash.forward(q, k, v)
+                ref_out = ref.qflash.forward(q, k, v, attn_mask=mask)
                 torch.cuda.synchronize()
                 compile_s = time.perf_counter() - t0
-                ours_out = K.qflash_forward(q, k, v)
+                ours_out = K.qflash_forward(q, k, v, attn_mask=mask)
                 exact = bool(torch.equal(ref_out, ours_out))
                 ndiff = int((ref_out != ours_out).sum())
                 del ref_out, ours_out
-                ref_ms = float(ref.qflash.forward(q, k, v, return_mode='latency'))
-                our_ms = float(K.qflash_forward(q, k, v, return_mode='latency'))
+                ref_ms = float(ref.qflash.forward(q, k, v, attn_mask=mask, return_mode='latency'))
+                our_ms = float(K.qflash_forward(q, k, v, attn_mask=mask, return_mode='latency'))
                 triton_ref = {"us_per_call": round(ref_ms * 1e3, 2), "ours_us_per_call_same_method": round(our_ms * 1e3, 2),
                               "ratio": round(ref_ms / our_ms, 3), "bit_exact_outputs": exact, "differing": ndiff,
                               "method": "reference qflash.forward(return_mode='latency'): triton do_bench median, "
@@ -484,17 +535,25 @@ def main():
     # batch (the reference's accuracy figure, benchmark.py:26-28), beside the
     # oracle's on the same int8 tensors
     sqnr = None
-    if world == 1 and win is None:
+    if world == 1:
         nz = max(1, min(w.Z, 4 * 12 * 197 // (w.H * w.N)))
+        if period:
+            nz = max(period, nz - nz % period)
+        mask_nz = None if mask is None else (mask if mask.shape[0] == 1 else mask[:nz])
         with torch.no_grad():
-            ref32 = torch.nn.functional.scaled_dot_product_attention(q[:nz], k[:nz], v[:nz])
+            ref32 = torch.nn.functional.scaled_dot_product_attention(q[:nz], k[:nz], v[:nz], attn_mask=mask_nz)
             ours = sets[0][3][:nz].float() * vs
             sqnr = {"sample": f"{nz} of {w.Z} batch entries ({nz * w.H} heads)", "vs": "fp32 scaled_dot_product_attention",
                     "ours_db": round(sqnr_db(ref32, ours), 4)}
             if not a.no_cpu:
                 from oracle import qflash_oracle as orc
+                bias_or = None
+                if bias is not None:
+                    zb = period or (w.Z if bstr[0] else 1)
+                    bias_or = torch.as_strided(bias, (zb, w.H, w.N, w.N), bstr).cpu().numpy()
+                    bias_or = bias_or[np.arange(nz) % zb]
                 o_or = orc.attention_int8(q8f[:nz].cpu().numpy(), k8f[:nz].cpu().numpy(), v8f[:nz].cpu().numpy(),
-                                          orc.Params(sm_scale, rs, eM, rM, lM, aM))
+                                          orc.Params(sm_scale, rs, eM, rM, lM, aM), bias=bias_or)
                 o_or = torch.from_numpy(o_or).to(dev).float() * vs
                 sqnr["oracle_db"] = round(sqnr_db(ref32, o_or), 4)
                 sqnr["abs_diff_db"] = round(abs(sqnr["ours_db"] - sqnr["oracle_db"]), 4)
@@ -519,16 +578,20 @@ def main():
             bias_n = torch.as_strided(bias, (zb, w.H, w.N, w.N), bstr).cpu().numpy()
             if period:
                 bias_n = bias_n[np.arange(w.Z) % period]
+            elif zb == 1:
+                bias_n = np.broadcast_to(bias_n, (w.Z, w.H, w.N, w.N))   # per-head tasks slice the batch
         procs = os.cpu_count() or 1
         zs, hs = cpu_sample_heads(q8n, k8n, v8n, prm, 2)
         t1, _ = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, 1, bias_n)
-        nh = int(max(procs, min(w.Z * w.H, a.cpu_seconds * procs / max(t1 / len(zs), 1e-6))))
+        nh = int(max(procs, a.cpu_seconds * procs / max(t1 / len(zs), 1e-6)))
         zs, hs = cpu_sample_heads(q8n, k8n, v8n, prm, nh, seed=1)
-        dt, outs = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs, bias_n)
-        ops = 4 * len(zs) * w.N * w.N * w.D
+        passes = max(1, min(64, round(nh / len(zs))))   # a small workload: the whole of it, several times
+        dt, outs = run_cpu_oracle(q8n, k8n, v8n, prm, zs, hs, procs, bias_n, passes)
+        ops = 4 * len(zs) * passes * w.N * w.N * w.D
         cpu = {"value": ops / dt / 1e12, "unit": "TOPS", "cores": procs, "kind": "port",
-               "sample": f"{len(zs)} of {w.Z * w.H} (z,h) heads of {w.name}, numpy oracle, {procs} processes, "
-                         f"{dt:.1f} s"}
+               "sample": f"{len(zs)} of the {w.Z * w.H} (z,h) heads of {w.name}"
+                         + (f" x {passes} passes" if passes > 1 else "")
+                         + f", numpy oracle, {procs} processes, {dt:.1f} s"}
         sample_exact = all(np.array_equal(o[0, 0], o_gpu[z, h]) for o, z, h in zip(outs, zs, hs))
 
     value = w.ops / (ms_step * 1e-3) / 1e12
@@ -539,6 +602,7 @@ def main():
     traffic = profile_traffic("qfa_fwd", w.name) if world == 1 else None
     clocks = clk.summary()
     if world > 1:
+        peer.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -561,8 +625,9 @@ def main():
         "config": {"workload": w.name, "Z": w.Z, "H": w.H, "N": w.N, "D": w.D, "bias_bytes": bias_bytes,
                    "division": "div.full (the reference's compiled kernel on B200; default)",
                    "l2": f"{n_sets} rotating input sets ({n_sets * shard_bytes / 1e6:.0f} MB > 126 MB L2)",
-                   "parallelism": (f"batch-sharded over {world} GPUs ({zl} of {w.Z} per rank) + NCCL all_gather "
-                                   f"of the int8 O shards inside every step" if world > 1 else "1 GPU"),
+                   "parallelism": (f"batch-sharded over {world} GPUs ({zl} of {w.Z} per rank); every step: "
+                                   f"all_reduce(MAX) of the scales, the attention kernel writing every rank's copy "
+                                   f"of the gathered int8 O, an ordering all_reduce" if world > 1 else "1 GPU"),
                    "grid_ctas": grid},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
@@ -581,9 +646,7 @@ def main():
         "cpu_baseline": cpu,
         "triton_ref": triton_ref,
         "sqnr": sqnr,
-        "multi_gpu": ({"kernel_ms": round(kernel_ms, 4), "gather_ms": round(gather_ms, 4),
-                       "step_ms": round(ms_step, 4), "gathered_bit_exact_vs_1gpu": multi_exact,
-                       "collective": "NCCL all_gather_into_tensor of the int8 O shards"} if world > 1 else None),
+        "multi_gpu": multi,
         "gpu_launches": int(launches),
         "clocks": clocks,
         "parity_sample_bit_exact": sample_exact,

@@ -82,6 +82,40 @@ int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* 
                      int32_t l_shift, int32_t acc_shift, uint32_t flags, void* stream);
 
 /*
+ * qflash_i8_fwd_ex for a batch shard whose int8 output is wanted on every GPU
+ * of a job (the all_gather of the shards, fused into the attention epilogue;
+ * no counterpart in the reference, whose multi-GPU use is data parallel over
+ * batches).  o points at this shard's rows inside a gathered [Z_total, H, N, D]
+ * buffer; o_peers[i] points at the same rows of another GPU's copy of that
+ * buffer, mapped into this process (qflash_ipc_open), with o's strides and
+ * o's 16-byte alignment.  Every O row is stored into o and into each peer copy
+ * (P2P stores over NVLink; nothing is read from peer memory).  The stores are
+ * performed system-wide before the kernel completes: a collective enqueued
+ * after this call on the same stream of every rank (e.g. an all_reduce of one
+ * element) orders them before any rank reads its copy.  0 <= n_peers <= 7;
+ * n_peers = 0 is qflash_i8_fwd_ex.
+ */
+int qflash_i8_fwd_gather(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                         const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
+                         const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H,
+                         int N, int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
+                         int32_t l_shift, int32_t acc_shift, uint32_t flags, int8_t* const* o_peers, int n_peers,
+                         void* stream);
+
+/*
+ * CUDA IPC for the gathered output: qflash_ipc_alloc allocates `bytes` of
+ * device memory on the current device and writes its 64-byte IPC handle;
+ * another process opens it with qflash_ipc_open (on its current device, peer
+ * access enabled) and unmaps it with qflash_ipc_close; the owner frees it with
+ * qflash_ipc_free once every peer has closed it.
+ */
+#define QFLASH_IPC_HANDLE_BYTES 64
+int qflash_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int qflash_ipc_open(const void* handle, void** ptr);
+int qflash_ipc_close(void* ptr);
+int qflash_ipc_free(void* ptr);
+
+/*
  * The whole forward of qflash.forward on the device, without the reference's
  * host synchronisation (the `.item()` at qflash/kernel.py:297): per-tensor
  * scales (kernel.py:294-296), the fixed-point constants (kernel.py:298-307,

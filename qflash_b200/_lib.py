@@ -36,6 +36,17 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p]),
+    "qflash_i8_fwd_gather": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        _I64x4, _I64x4, _I64x4, _I64x4, _I64x4, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+        ctypes.c_void_p]),
+    "qflash_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
+    "qflash_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "qflash_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "qflash_ipc_free": (ctypes.c_int, [ctypes.c_void_p]),
     "qflash_fwd_fused": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, _I64x4, _I64x4, _I64x4,
         ctypes.c_void_p, ctypes.c_int, _I64x4, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -110,15 +121,50 @@ def _check(rc: int, what: str):
 
 
 def i8_fwd(q, k, v, o, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
-           l_shift, acc_shift, flags, stream, bias_z_period=0) -> None:
-    """Launch the attention kernel on device tensors (no synchronisation)."""
+           l_shift, acc_shift, flags, stream, bias_z_period=0, o_peers=None) -> None:
+    """Launch the attention kernel on device tensors (no synchronisation).
+    ``o_peers``: device addresses (ints) of o's rows in other GPUs' copies of
+    the gathered output (qflash_i8_fwd_gather)."""
     lib = load()
     bs = (ctypes.c_int64 * 4)(*bias_strides) if bias is not None else None
-    rc = lib.qflash_i8_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                              bias.data_ptr() if bias is not None else None,
-                              _strides(q), _strides(k), _strides(v), _strides(o), bs, bias_z_period,
-                              Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags, stream)
-    _check(rc, "qflash_i8_fwd_ex")
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), bias.data_ptr() if bias is not None else None,
+            _strides(q), _strides(k), _strides(v), _strides(o), bs, bias_z_period,
+            Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags)
+    if o_peers:
+        peers = (ctypes.c_void_p * len(o_peers))(*[int(p) for p in o_peers])
+        _check(lib.qflash_i8_fwd_gather(*args, peers, len(o_peers), stream), "qflash_i8_fwd_gather")
+    else:
+        _check(lib.qflash_i8_fwd_ex(*args, stream), "qflash_i8_fwd_ex")
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Device memory on the current device that other processes can map:
+    (address, 64-byte CUDA IPC handle)."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(load().qflash_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "qflash_ipc_alloc")
+    return int(ptr.value), handle.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map another process's qflash_ipc_alloc buffer; returns its address here."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle has {IPC_HANDLE_BYTES} bytes, got {len(handle)}")
+    ptr = ctypes.c_void_p()
+    _check(load().qflash_ipc_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr)),
+           "qflash_ipc_open")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(load().qflash_ipc_close(ptr), "qflash_ipc_close")
+
+
+def ipc_free(ptr: int) -> None:
+    _check(load().qflash_ipc_free(ptr), "qflash_ipc_free")
 
 
 DTYPES = {"torch.float32": 0, "torch.float16": 1, "torch.bfloat16": 2, "torch.bool": 3}

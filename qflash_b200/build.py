@@ -18,7 +18,8 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libqflash_b200.so"
-SOURCES = [CSRC / "qflash_fwd.cu", CSRC / "qflash_quant.cu", CSRC / "qflash_noalloc.cu", CSRC / "qflash_peak.cu"]
+SOURCES = [CSRC / "qflash_fwd.cu", CSRC / "qflash_quant.cu", CSRC / "qflash_noalloc.cu", CSRC / "qflash_peak.cu",
+           CSRC / "qflash_peer.cu"]
 HEADERS = [CSRC / "sm100_ptx.cuh", CSRC / "qfb_internal.h", PKG.parent / "include" / "qflash_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v"]

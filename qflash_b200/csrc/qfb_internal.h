@@ -58,6 +58,19 @@ struct DeviceGuard {
   DeviceGuard& operator=(const DeviceGuard&) = delete;
 };
 int select_device(const void* p, int* dev);
+
+// Copies of the int8 output tensor in other GPUs' memory (CUDA IPC mappings of
+// the same [Z, H, N, D] layout): the attention epilogue stores every O row into
+// o and into each peer copy at the same offset (an all-gather fused into the
+// kernel).  n <= kMaxPeers.
+constexpr int kMaxPeers = 7;
+// signal words of the gather barrier: one flag per rank, then the finished-CTA counter
+constexpr int kSigCount = kMaxPeers + 1;
+constexpr int kSigWords = kSigCount + 1;
+struct PeerSpec {
+  int n;
+  int8_t* o[kMaxPeers];
+};
 int sm_count(int dev);
 
 // The attention launch behind qflash_i8_fwd_ex; with `dparams` the fixed-point
@@ -66,7 +79,8 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
                   const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
                   const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N,
                   int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
-                  int32_t acc_shift, uint32_t flags, const long long* dparams, const OutSpec* out, void* stream);
+                  int32_t acc_shift, uint32_t flags, const long long* dparams, const OutSpec* out, void* stream,
+                  const PeerSpec* peers = nullptr);
 
 
 // The on-device forward behind qflash_fwd_fused and the workspace it needs.

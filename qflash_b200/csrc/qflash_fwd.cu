@@ -51,7 +51,7 @@ __device__ unsigned int g_err;       // set when a bounded wait gives up
 
 // Error codes written to g_err (bit set per site).
 enum : unsigned { kErrQEmpty = 1, kErrKvEmpty = 2, kErrQFull = 4, kErrKvFull = 8, kErrPFull = 16,
-                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128, kErrSelftest = 1u << 31 };
+                  kErrPvEmpty = 32, kErrSFull = 64, kErrPvFull = 128, kErrPeer = 256, kErrSelftest = 1u << 31 };
 
 struct KArgs {
   int Z, H, N, nch, ntiles, nitems, ZH;
@@ -78,6 +78,19 @@ struct KArgs {
   long long ou_z, ou_h, ou_n;
   int out_dtype, out_vec16;
   float o_scale;
+  // int8 O rows are also stored at these byte offsets from their address in o:
+  // the same tensor in other GPUs' memory (PeerSpec), written over NVLink
+  int n_peer;
+  long long o_peer_off[kMaxPeers];
+  int o_bulk;                // a warp's O rows are contiguous: staged in shared memory, written by bulk copies
+  // Gather barrier (when sig is set): the last CTA to finish stores `epoch`
+  // into slot sig_rank of every rank's signal words and waits (bounded) until
+  // all sig_world slots of its own hold it, so the kernel completes only once
+  // every rank's rows are in every copy.  sig[kSigCount] counts finished CTAs.
+  uint32_t* sig;
+  uint32_t* sig_peer[kMaxPeers];
+  int sig_rank, sig_world;
+  uint32_t epoch;
 };
 
 // ------------------------------------------------------------------ integer primitives
@@ -282,7 +295,10 @@ struct Cfg {
   static constexpr int OFF_V = OFF_K + KVS * K_BYTES;
   static constexpr int OFF_V2 = OFF_V + KVS * V_BYTES;
   static constexpr int OFF_B = OFF_V2 + KVS * V2_BYTES;
-  static constexpr int OFF_BAR = OFF_B + KVS * B_BYTES;
+  // int8 O rows of each softmax warp, staged for bulk copies (gathered output)
+  static constexpr int STG_BYTES = DV <= 64 ? 4 * 32 * DV : 0;
+  static constexpr int OFF_STG = OFF_B + KVS * B_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2;
   static constexpr int THREADS = kThreads;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
@@ -942,7 +958,17 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
             for (int i = 0; i < 16; ++i) v[2 * i] ^= (int)0x80000000u;  // unbias
           }
           uint32_t res[EPP / 4];
-          if (div_full || fast_ieee) {
+          bool part_fast = div_full || fast_ieee;
+          if (!part_fast) {
+            // IEEE rounding without a bound for the row (e.g. a negative P byte
+            // stopped the l-based bound): the fast form still holds for this
+            // part if its own values have |acc| < 2^23
+            bool in_range = l > 0 && l < (1 << 24);
+#pragma unroll
+            for (int i = 0; i < EPP; ++i) in_range = in_range && (unsigned)(v[STEP * i] + 8388607) <= 16777214u;
+            part_fast = __all_sync(0xffffffffu, in_range || !row_ok);
+          }
+          if (part_fast) {
             int r[EPP];
 #pragma unroll
             for (int i = 0; i < EPP; ++i) {
@@ -981,19 +1007,32 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
                              part * EPP) * esz;
             store_dequant<EPP>(drow, res, k_os, a.out_dtype, a.out_vec16);
           } else if (row_ok) {
+            int8_t* dst = orow + part * EPP;
             if (a.o_vec16) {
 #pragma unroll
-              for (int q4 = 0; q4 < EPP / 16; ++q4)
-                *(int4*)(orow + part * EPP + 16 * q4) = make_int4((int)res[4 * q4], (int)res[4 * q4 + 1],
-                                                                   (int)res[4 * q4 + 2], (int)res[4 * q4 + 3]);
+              for (int q4 = 0; q4 < EPP / 16; ++q4) {
+                const int4 val = make_int4((int)res[4 * q4], (int)res[4 * q4 + 1], (int)res[4 * q4 + 2],
+                                           (int)res[4 * q4 + 3]);
+                *(int4*)(dst + 16 * q4) = val;
+#pragma unroll 1
+                for (int pi = 0; pi < a.n_peer; ++pi) *(int4*)(dst + a.o_peer_off[pi] + 16 * q4) = val;
+              }
             } else {
 #pragma unroll
-              for (int b = 0; b < EPP; ++b) orow[part * EPP + b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
+              for (int b = 0; b < EPP; ++b) dst[b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
+#pragma unroll 1
+              for (int pi = 0; pi < a.n_peer; ++pi)
+#pragma unroll
+                for (int b = 0; b < EPP; ++b) dst[a.o_peer_off[pi] + b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
             }
           }
         }
       }
     }
+    // the peer copies' rows are performed system-wide before the kernel
+    // completes, so whatever follows it in stream order (the barrier
+    // collective) orders them before any reader on the other GPUs
+    if (a.n_peer > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -1203,7 +1242,8 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
                   const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
                   const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N,
                   int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M, int32_t l_shift,
-                  int32_t acc_shift, uint32_t flags, const long long* dparams, const OutSpec* out, void* stream_) {
+                  int32_t acc_shift, uint32_t flags, const long long* dparams, const OutSpec* out, void* stream_,
+                  const PeerSpec* peers) {
   cudaStream_t stream = (cudaStream_t)stream_;
   if (Z < 0 || H < 0 || N < 0) return set_err(QFLASH_ERR_ARG, "negative shape");
   if (!(D == 32 || D == 64 || D == 128 || D == 256)) return set_err(QFLASH_ERR_ARG, "head dim %d not in {32,64,128,256}", D);
@@ -1261,6 +1301,24 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
     ka.os_n = o_strides[2];
     ka.o_vec16 = (((uintptr_t)o & 15) == 0) && (o_strides[0] % 16 == 0) && (o_strides[1] % 16 == 0) &&
                  (o_strides[2] % 16 == 0);
+  }
+  if (peers && peers->n > 0) {
+    if (fused_out) return set_err(QFLASH_ERR_UNSUPPORTED, "peer copies take the int8 output only");
+    if (peers->n > kMaxPeers) return set_err(QFLASH_ERR_ARG, "%d peer copies (at most %d)", peers->n, kMaxPeers);
+    for (int i = 0; i < peers->n; ++i) {
+      const int8_t* po = peers->o[i];
+      if (!po) return set_err(QFLASH_ERR_ARG, "peer copy %d is null", i);
+      // same 16-byte phase as o, so the vector stores stay aligned in every copy
+      if (((uintptr_t)po & 15) != ((uintptr_t)o & 15))
+        return set_err(QFLASH_ERR_ALIGN, "peer copy %d (%p) and o (%p) differ in 16-byte alignment", i, po, o);
+      cudaPointerAttributes pa;
+      if (cudaPointerGetAttributes(&pa, po) != cudaSuccess || pa.type != cudaMemoryTypeDevice) {
+        cudaGetLastError();
+        return set_err(QFLASH_ERR_ARG, "peer copy %d (%p) is not device memory known to CUDA", i, po);
+      }
+      ka.o_peer_off[i] = (long long)((intptr_t)po - (intptr_t)o);
+    }
+    ka.n_peer = peers->n;
   }
   ka.rs = sm_rscale;
   ka.eM = exp_M;
@@ -1368,6 +1426,24 @@ extern "C" int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* 
   return qfb::attention_fwd(q, k, v, o, bias, q_strides, k_strides, v_strides, o_strides, bias_strides,
                             bias_z_period, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags,
                             nullptr, nullptr, stream);
+}
+
+extern "C" int qflash_i8_fwd_gather(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
+                                    const int64_t q_strides[4], const int64_t k_strides[4],
+                                    const int64_t v_strides[4], const int64_t o_strides[4],
+                                    const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N, int D,
+                                    int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
+                                    int32_t l_shift, int32_t acc_shift, uint32_t flags, int8_t* const* o_peers,
+                                    int n_peers, void* stream) {
+  if (n_peers < 0 || n_peers > qfb::kMaxPeers || (n_peers > 0 && !o_peers))
+    return qfb::set_err(QFLASH_ERR_ARG, "n_peers %d (0..%d, with a pointer array)", n_peers, qfb::kMaxPeers);
+  qfb::PeerSpec ps;
+  memset(&ps, 0, sizeof(ps));
+  ps.n = n_peers;
+  for (int i = 0; i < n_peers; ++i) ps.o[i] = o_peers[i];
+  return qfb::attention_fwd(q, k, v, o, bias, q_strides, k_strides, v_strides, o_strides, bias_strides,
+                            bias_z_period, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags,
+                            nullptr, nullptr, stream, &ps);
 }
 
 extern "C" int qflash_i8_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,

@@ -152,9 +152,11 @@ def do_bench(fn, warmup: float = 10, rep: float = 100) -> float:
 def launch_int8(q8: Tensor, k8: Tensor, v8: Tensor, o8: Tensor, sm_rscale: int, exp_M: int, req_M: int,
                 l_M: int, acc_M: int, bias: Tensor | None = None, bias_strides=None,
                 l_shift: int = None, acc_shift: int = None, flags: int = None, stream=None,
-                bias_z_period: int = 0) -> None:
+                bias_z_period: int = 0, o_peers=None) -> None:
     """Run the sm_100a kernel on int8 [Z, H, N, D] tensors already on the GPU
-    (the launch at qflash/kernel.py:319-326 / 339-346)."""
+    (the launch at qflash/kernel.py:319-326 / 339-346).  ``o_peers``: addresses
+    of o8's rows in other GPUs' copies of a gathered output (``shard.PeerOutput``),
+    which the epilogue fills as well."""
     for t in (q8, k8, v8, o8):
         if not t.is_cuda or t.dtype != torch.int8 or t.dim() != 4:
             raise ValueError("q, k, v, o must be 4-D int8 CUDA tensors")
@@ -166,7 +168,7 @@ def launch_int8(q8: Tensor, k8: Tensor, v8: Tensor, o8: Tensor, sm_rscale: int, 
             raise OverflowError(f"{name}={val} does not fit in int32")
     _lib.i8_fwd(q8, k8, v8, o8, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
                 L_SHIFT if l_shift is None else l_shift, ACC_SHIFT if acc_shift is None else acc_shift,
-                arith_flags() if flags is None else flags, stream, bias_z_period)
+                arith_flags() if flags is None else flags, stream, bias_z_period, o_peers)
 
 
 def qflash_forward(
@@ -294,14 +296,18 @@ def tensor_scales(query: Tensor, key: Tensor, value: Tensor):
 
 
 def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mode='output',
-                        scales=None, launch=None, return_int8=False, bias_z_period=0):
-    """The body of ``qflash.forward`` with two seams: ``scales`` supplies
+                        scales=None, launch=None, return_int8=False, bias_z_period=0,
+                        o_out=None, o_peers=None, dequant=True):
+    """The body of ``qflash.forward`` with seams: ``scales`` supplies
     (q_scale, k_scale, o_scale) computed elsewhere (the sharded path reduces
     them over all ranks so each shard quantises exactly like the whole
     tensor), ``launch`` replaces the kernel launch (host-logic tests), and
     ``return_int8`` also returns (o8, o_scale); ``bias_z_period`` > 0 means
     ``attn_mask`` has that many batch entries and batch z uses entry
-    z % bias_z_period (see ``window_attention``)."""
+    z % bias_z_period (see ``window_attention``).  ``o_out`` is the int8 output
+    tensor to write (default: a new one), ``o_peers`` the addresses of its rows
+    in other GPUs' copies (``shard.PeerOutput``), and ``dequant=False`` skips
+    the local ``o * o_scale`` (returned as None)."""
     HEAD_DIM_Q, HEAD_DIM_K = query.shape[-1], key.shape[-1]
     HEAD_DIM_V = value.shape[-1]
     assert HEAD_DIM_Q == HEAD_DIM_K and HEAD_DIM_K == HEAD_DIM_V
@@ -321,7 +327,12 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
     value = quantize(value, o_scale)
     # the TMA loads need the head dim innermost (the reference takes any strides)
     query, key, value = (t if t.stride(-1) == 1 else t.contiguous() for t in (query, key, value))
-    o = torch.empty_like(value)
+    if o_out is None:
+        o = torch.empty_like(value)
+    else:
+        if o_out.dtype != torch.int8 or o_out.shape != value.shape or o_out.stride(-1) != 1:
+            raise ValueError(f"o_out must be int8 {tuple(value.shape)} with the head dim contiguous")
+        o = o_out
 
     Z, H, N = query.shape[0], query.shape[1], query.shape[2]
     bias, bias_strides = None, None
@@ -333,14 +344,15 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
             launch(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides)
         else:
             launch_int8(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides,
-                        bias_z_period=bias_z_period)
+                        bias_z_period=bias_z_period, o_peers=o_peers)
 
     if return_mode == 'latency':
         return do_bench(kernel, warmup=10, rep=100)
     kernel()
+    out = o * o_scale if dequant else None
     if return_int8:
-        return o * o_scale, o, o_scale
-    return o * o_scale
+        return out, o, o_scale
+    return out
 
 
 def forward_window_fused(query, key, value, table, index, window_mask=None, scale=None, check=True, out=None):

@@ -7,15 +7,23 @@ communication.  The only subtlety is the per-tensor quantisation scale
 reduce their local |Q|, |K|, |V| maxima with one all_reduce(MAX) of three
 scalars before quantising -- after that every shard's int8 values and
 fixed-point constants are bit-identical to what a single process computes on
-the full tensor.  ``gather=True`` collects the int8 outputs on every rank
-with all_gather (the result a scaling run checks); nothing else crosses GPUs.
+the full tensor.  ``gather=True`` collects the int8 outputs on every rank:
+with a ``PeerOutput`` the attention epilogue itself stores every row into
+every rank's copy of the gathered output over NVLink (one small all_reduce
+afterwards orders those stores before any rank reads), otherwise NCCL
+all_gather runs after the kernel; nothing else crosses GPUs.
 """
 from __future__ import annotations
+
+import math
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .kernel import forward_with_scales, tensor_scales
+
+MAX_RANKS = 8   # the epilogue stores into at most 7 peer copies
 
 
 def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -41,19 +49,97 @@ def global_scales(query, key, value, group=None):
     return tuple(local[i].to(dt) / i8max for i in range(3))
 
 
-def forward_sharded(query, key, value, attn_mask=None, scale=None, group=None, gather=False, launch=None):
+class _CudaArray:
+    """A raw int8 device buffer exposed through ``__cuda_array_interface__``,
+    which ``torch.as_tensor`` wraps without a copy."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "|i1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerOutput:
+    """The gathered int8 output [Z, H, N, D] of a batch-sharded attention, one
+    copy on every rank, mapped into every other rank's process (CUDA IPC), so
+    that each rank's attention epilogue stores its shard's rows into all the
+    copies at once (``qflash_i8_fwd_gather``).  Collective: every rank of
+    ``group`` creates it with the same shape (on its current CUDA device) and
+    calls ``close()``.  ``buffer`` is this rank's copy; a call of
+    ``forward_sharded(..., gather=True, peer_out=...)`` overwrites it."""
+
+    def __init__(self, shape, group=None):
+        if not (dist.is_available() and dist.is_initialized()):
+            raise RuntimeError("PeerOutput needs an initialised process group")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > MAX_RANKS:
+            raise ValueError(f"{self.world} ranks: the fused gather takes at most {MAX_RANKS}")
+        self.shape = tuple(int(x) for x in shape)
+        if len(self.shape) != 4:
+            raise ValueError("PeerOutput holds a [Z, H, N, D] tensor")
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self._ptr, handle = _lib.ipc_alloc(max(1, math.prod(self.shape)))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self._peers = [_lib.ipc_open(h) for r, h in enumerate(handles) if r != self.rank]
+        self.buffer = torch.as_tensor(_CudaArray(self._ptr, self.shape), device=self.device)
+        if self.buffer.data_ptr() != self._ptr:
+            raise RuntimeError("the gathered buffer was copied instead of wrapped")
+
+    def peer_rows(self, z0: int) -> list[int]:
+        """Addresses of batch entry z0 in every other rank's copy."""
+        row = math.prod(self.shape[1:])
+        return [p + z0 * row for p in self._peers]
+
+    def close(self):
+        """Unmap the peers' copies and free this one (collective)."""
+        if self._ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)          # every rank's stores into every copy are done
+        for p in self._peers:
+            _lib.ipc_close(p)
+        dist.barrier(group=self.group)          # no rank maps this copy any more
+        self.buffer = None
+        _lib.ipc_free(self._ptr)
+        self._ptr, self._peers = None, []
+
+
+def forward_sharded(query, key, value, attn_mask=None, scale=None, group=None, gather=False, launch=None,
+                    peer_out: PeerOutput | None = None):
     """``qflash.forward`` on this rank's batch shard [Zl, H, N, D].
 
     attn_mask, if given, is this shard's mask (batch dimension sliced the same
     way, or broadcast with batch size 1).  Returns the dequantised local
     output, or with ``gather=True`` the full [Z, H, N, D] output assembled
-    from every rank's int8 shard."""
+    from every rank's int8 shard -- written by the attention epilogue into
+    ``peer_out`` on every rank when given (shards in rank order), else
+    collected with NCCL all_gather."""
     scales = global_scales(query, key, value, group)
+    world = dist.get_world_size(group)
+    if gather and peer_out is not None:
+        sizes = torch.tensor([query.shape[0]], device=query.device)
+        all_sizes = [torch.zeros_like(sizes) for _ in range(world)]
+        dist.all_gather(all_sizes, sizes, group=group)
+        all_sizes = [int(s.item()) for s in all_sizes]
+        rank = dist.get_rank(group)
+        z0 = sum(all_sizes[:rank])
+        if peer_out.shape != (sum(all_sizes),) + tuple(query.shape[1:]):
+            raise ValueError(f"peer_out holds {peer_out.shape}, the shards make "
+                             f"{(sum(all_sizes),) + tuple(query.shape[1:])}")
+        o_local = peer_out.buffer[z0:z0 + query.shape[0]]
+        _, _, o_scale = forward_with_scales(query, key, value, attn_mask, scale, scales=scales, launch=launch,
+                                            return_int8=True, o_out=o_local, o_peers=peer_out.peer_rows(z0),
+                                            dequant=False)
+        # every rank's kernel precedes its part of this collective in stream
+        # order, so after it all peer stores into this rank's copy are done
+        dist.all_reduce(torch.zeros(1, device=query.device), group=group)
+        return peer_out.buffer * o_scale
     out, o8, o_scale = forward_with_scales(query, key, value, attn_mask, scale, scales=scales,
                                            launch=launch, return_int8=True)
     if not gather:
         return out
-    world = dist.get_world_size(group)
     sizes = torch.tensor([o8.shape[0]], device=o8.device)
     all_sizes = [torch.zeros_like(sizes) for _ in range(world)]
     dist.all_gather(all_sizes, sizes, group=group)

@@ -1,4 +1,6 @@
-"""Batch-sharded forward over 2 GPUs (NCCL) equals the single-GPU forward bit for bit."""
+"""Batch-sharded forward over 2 GPUs equals the single-GPU forward bit for bit,
+with the result gathered by NCCL all_gather or by the attention epilogue's
+stores into every rank's copy (PeerOutput)."""
 import os
 import socket
 import tempfile
@@ -16,9 +18,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, path):
+def _worker(rank, world, port, path, fused):
     import torch.distributed as dist
-    from qflash_b200.shard import forward_sharded, shard_bounds
+    from qflash_b200.shard import PeerOutput, forward_sharded, shard_bounds
     from qflash_b200.workloads import WORKLOADS, make_inputs
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -29,23 +31,31 @@ def _worker(rank, world, port, path):
     w = WORKLOADS["vit_b"].scaled(7)
     q, k, v, _ = make_inputs(w, seed=3, device=dev)       # every rank builds the full tensors ...
     a, b = shard_bounds(w.Z, world, rank)                # ... and takes its batch slice
-    out = forward_sharded(q[a:b].contiguous(), k[a:b].contiguous(), v[a:b].contiguous(), gather=True)
+    peer = PeerOutput(q.shape) if fused else None
+    outs = []
+    for _ in range(2):   # a second call overwrites the gathered copies
+        outs.append(forward_sharded(q[a:b].contiguous(), k[a:b].contiguous(), v[a:b].contiguous(), gather=True,
+                                    peer_out=peer).cpu())
     torch.cuda.synchronize()
-    torch.save(out.cpu(), os.path.join(path, f"r{rank}.pt"))
+    torch.save(outs, os.path.join(path, f"r{rank}.pt"))
+    if peer is not None:
+        peer.close()
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_forward_two_gpus_bit_exact():
+@pytest.mark.parametrize("fused", [False, True], ids=["nccl_all_gather", "epilogue_peer_stores"])
+def test_sharded_forward_two_gpus_bit_exact(fused):
     import torch.multiprocessing as mp
     from qflash_b200 import qflash
     from qflash_b200.workloads import WORKLOADS, make_inputs
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(2, _free_port(), d), nprocs=2, start_method="spawn", join=True)
+        mp.start_processes(_worker, args=(2, _free_port(), d, fused), nprocs=2, start_method="spawn", join=True)
         outs = [torch.load(os.path.join(d, f"r{r}.pt")) for r in range(2)]
     w = WORKLOADS["vit_b"].scaled(7)
     q, k, v, _ = make_inputs(w, seed=3, device="cuda:0")
     ref = qflash.forward(q, k, v).cpu()
-    for o in outs:
-        assert torch.equal(o, ref)
+    for per_rank in outs:
+        for o in per_rank:
+            assert torch.equal(o, ref)

@@ -118,3 +118,11 @@ def test_dead_peer_raises_instead_of_hanging():
         assert not alive, "a rank hung"
         with open(os.path.join(d, "r0.txt")) as f:
             assert f.read().startswith("raised")
+
+
+def test_peer_output_needs_a_process_group():
+    from qflash_b200.shard import PeerOutput
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised")
+    with pytest.raises(RuntimeError, match="process group"):
+        PeerOutput((2, 3, 40, 32))
