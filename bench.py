@@ -253,7 +253,6 @@ def main():
         peer_dst, peer_rows = peer.buffer[z0:z1], peer.peer_rows(z0)
         # this rank's |max| of its float Q/K/V shards: the global-scale reduction of forward_sharded
         amax3 = torch.stack([t[z0:z1].abs().amax().float() for t in (q, k, v)])
-        sync1 = torch.zeros(1, device=dev)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
@@ -263,15 +262,11 @@ def main():
         K.launch_int8(s[0], s[1], s[2], s[3], rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period)
 
     def kernel_gather(i):
-        # the attention kernel storing its rows into every rank's gathered copy
+        # the attention kernel storing its rows into every rank's gathered copy;
+        # it completes once every rank's rows are in every copy (its own barrier)
         s = sets[i % n_sets]
         K.launch_int8(s[0], s[1], s[2], peer_dst, rs, eM, rM, lM, aM, bias, bstr, stream=sp, bias_z_period=period,
-                      o_peers=peer_rows)
-
-    def order():
-        # every rank's kernel precedes its part of this collective: afterwards
-        # all peer stores into this rank's copy are done
-        dist.all_reduce(sync1)
+                      o_peers=peer_rows, barrier=peer.next_barrier())
 
     def gather(i):
         o = sets[i % n_sets][3]
@@ -282,9 +277,8 @@ def main():
 
     def step(i):
         if world > 1:
-            dist.all_reduce(amax3, op=dist.ReduceOp.MAX)   # global scales (3 scalars)
+            peer.max_(amax3)     # global scales: max of 3 scalars over the ranks, through peer memory
             kernel_gather(i)
-            order()
         else:
             kernel(i)
 
@@ -341,16 +335,18 @@ def main():
     if world > 1:
         multi = {"kernel_ms": round(kernel_ms, 4),
                  "kernel_local_only_ms": round(timed(kernel, min(a.steps, 200)), 4),
-                 "order_allreduce_ms": round(timed(lambda i: order(), min(a.steps, 200)), 4),
+                 "scale_exchange_ms": round(timed(lambda i: peer.max_(amax3), min(a.steps, 200)), 4),
                  "scale_allreduce_ms": round(timed(lambda i: dist.all_reduce(amax3, op=dist.ReduceOp.MAX),
                                                    min(a.steps, 200)), 4),
                  "step_ms": round(ms_step, 4),
                  "nccl_gather_ms": round(timed(gather, min(a.steps, 50)), 4),
                  "nccl_step_ms": round(timed(step_nccl, min(a.steps, 100)), 4),
-                 "collective": "the attention epilogue stores every O row into every rank's copy of the gathered "
-                               "output (CUDA IPC mappings, P2P stores over NVLink), then a 1-element NCCL "
-                               "all_reduce orders those stores; nccl_step_ms: the same step with NCCL "
-                               "all_gather_into_tensor after a local-only kernel"}
+                 "collective": "scales: max of 3 scalars exchanged through the ranks' signal words "
+                               "(qflash_peer_max); output: the attention epilogue writes every warp's O rows into "
+                               "every rank's copy of the gathered output (CUDA IPC mappings, bulk copies over "
+                               "NVLink) and the kernel ends with a barrier over the ranks (flags in the peers' "
+                               "memory); nccl_step_ms: NCCL all_reduce of the scales, a local-only kernel, NCCL "
+                               "all_gather_into_tensor"}
 
     # the gathered output (both collectives) equals the single-GPU output bit for bit
     multi_exact = None
@@ -626,8 +622,9 @@ def main():
                    "division": "div.full (the reference's compiled kernel on B200; default)",
                    "l2": f"{n_sets} rotating input sets ({n_sets * shard_bytes / 1e6:.0f} MB > 126 MB L2)",
                    "parallelism": (f"batch-sharded over {world} GPUs ({zl} of {w.Z} per rank); every step: "
-                                   f"all_reduce(MAX) of the scales, the attention kernel writing every rank's copy "
-                                   f"of the gathered int8 O, an ordering all_reduce" if world > 1 else "1 GPU"),
+                                   f"the scales' max over the ranks, then the attention kernel writing every rank's "
+                                   f"copy of the gathered int8 O and ending with a barrier over the ranks"
+                                   if world > 1 else "1 GPU"),
                    "grid_ctas": grid},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,

@@ -89,27 +89,50 @@ int qflash_i8_fwd_ex(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* 
  * buffer; o_peers[i] points at the same rows of another GPU's copy of that
  * buffer, mapped into this process (qflash_ipc_open), with o's strides and
  * o's 16-byte alignment.  Every O row is stored into o and into each peer copy
- * (P2P stores over NVLink; nothing is read from peer memory).  The stores are
- * performed system-wide before the kernel completes: a collective enqueued
- * after this call on the same stream of every rank (e.g. an all_reduce of one
- * element) orders them before any rank reads its copy.  0 <= n_peers <= 7;
+ * (P2P stores over NVLink, bulk copies of whole warps' rows when the rows are
+ * dense and D <= 64; nothing is read from peer memory).  0 <= n_peers <= 7;
  * n_peers = 0 is qflash_i8_fwd_ex.
+ * With sig set, the kernel also completes only once every rank's rows are in
+ * every copy: sig points at this rank's QFLASH_SIG_WORDS signal words (uint32,
+ * zero-initialised, in memory the peers map), sig_peers[i] at the signal words
+ * of the rank that owns o_peers[i], rank is this rank's index in [0, n_peers],
+ * and epoch is a non-zero launch counter, equal on every rank for the same
+ * launch and growing from one launch to the next.  The last CTA to finish
+ * writes epoch into every rank's flag `rank` and waits (bounded, ~2 s; a
+ * timeout sets bit 256 of the device error word) until its own flags all
+ * reach epoch.  Launches of one rank must not overlap on its GPU.  With
+ * sig == NULL the caller orders the stores itself (a collective enqueued
+ * after this call on every rank, e.g. an all_reduce of one element).
  */
+#define QFLASH_SIG_WORDS 128
 int qflash_i8_fwd_gather(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, const int32_t* bias,
                          const int64_t q_strides[4], const int64_t k_strides[4], const int64_t v_strides[4],
                          const int64_t o_strides[4], const int64_t bias_strides[4], int bias_z_period, int Z, int H,
                          int N, int D, int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
                          int32_t l_shift, int32_t acc_shift, uint32_t flags, int8_t* const* o_peers, int n_peers,
-                         void* stream);
+                         uint32_t* sig, uint32_t* const* sig_peers, int rank, uint32_t epoch, void* stream);
 
 /*
  * CUDA IPC for the gathered output: qflash_ipc_alloc allocates `bytes` of
- * device memory on the current device and writes its 64-byte IPC handle;
+ * zeroed device memory on the current device and writes its 64-byte IPC handle;
  * another process opens it with qflash_ipc_open (on its current device, peer
  * access enabled) and unmaps it with qflash_ipc_close; the owner frees it with
  * qflash_ipc_free once every peer has closed it.
  */
 #define QFLASH_IPC_HANDLE_BYTES 64
+
+/*
+ * Max over the ranks of n <= 4 floats (device pointers in / out), through the
+ * same signal words as qflash_i8_fwd_gather's barrier (16-byte aligned): each
+ * rank writes its values and a flag into every rank's words and waits,
+ * bounded (~2 s; a timeout sets bit 256 of the device error word and writes
+ * NaN), for all flags of this epoch.  NaN wins, as in torch's amax.  Used for
+ * the global quantisation scales of a sharded forward (one launch of one
+ * thread instead of a library all_reduce).  epoch as for the gather barrier,
+ * counted separately from it.
+ */
+int qflash_peer_max(const float* in, int n, float* out, uint32_t* sig, uint32_t* const* sig_peers, int n_peers,
+                    int rank, uint32_t epoch, void* stream);
 int qflash_ipc_alloc(size_t bytes, void** ptr, void* handle);
 int qflash_ipc_open(const void* handle, void** ptr);
 int qflash_ipc_close(void* ptr);

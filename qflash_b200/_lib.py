@@ -42,7 +42,10 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
-        ctypes.c_void_p]),
+        ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
+    "qflash_peer_max": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
+        ctypes.c_int, ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
     "qflash_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
     "qflash_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     "qflash_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
@@ -121,23 +124,37 @@ def _check(rc: int, what: str):
 
 
 def i8_fwd(q, k, v, o, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
-           l_shift, acc_shift, flags, stream, bias_z_period=0, o_peers=None) -> None:
+           l_shift, acc_shift, flags, stream, bias_z_period=0, o_peers=None, barrier=None) -> None:
     """Launch the attention kernel on device tensors (no synchronisation).
     ``o_peers``: device addresses (ints) of o's rows in other GPUs' copies of
-    the gathered output (qflash_i8_fwd_gather)."""
+    the gathered output; ``barrier``: (sig, sig_peers, rank, epoch) of the
+    gather barrier inside the kernel (qflash_i8_fwd_gather)."""
     lib = load()
     bs = (ctypes.c_int64 * 4)(*bias_strides) if bias is not None else None
     args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), bias.data_ptr() if bias is not None else None,
             _strides(q), _strides(k), _strides(v), _strides(o), bs, bias_z_period,
             Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags)
-    if o_peers:
-        peers = (ctypes.c_void_p * len(o_peers))(*[int(p) for p in o_peers])
-        _check(lib.qflash_i8_fwd_gather(*args, peers, len(o_peers), stream), "qflash_i8_fwd_gather")
+    if o_peers or barrier:
+        o_peers = list(o_peers or [])
+        peers = (ctypes.c_void_p * max(1, len(o_peers)))(*[int(p) for p in o_peers])
+        sig, sig_peers, rank, epoch = barrier if barrier else (None, [], 0, 0)
+        sp = (ctypes.c_void_p * max(1, len(sig_peers)))(*[int(p) for p in sig_peers])
+        _check(lib.qflash_i8_fwd_gather(*args, peers, len(o_peers), sig, sp, rank, epoch, stream),
+               "qflash_i8_fwd_gather")
     else:
         _check(lib.qflash_i8_fwd_ex(*args, stream), "qflash_i8_fwd_ex")
 
 
 IPC_HANDLE_BYTES = 64
+SIG_WORDS = 128
+
+
+def peer_max(inp, out, sig: int, sig_peers, rank: int, epoch: int, stream) -> None:
+    """out[:n] = max over the ranks of inp[:n] (float32 device tensors, n <= 4)
+    through the ranks' signal words (qflash_peer_max); no synchronisation."""
+    sp = (ctypes.c_void_p * max(1, len(sig_peers)))(*[int(p) for p in sig_peers])
+    _check(load().qflash_peer_max(inp.data_ptr(), inp.numel(), out.data_ptr(), sig, sp, len(sig_peers), rank, epoch,
+                                  stream), "qflash_peer_max")
 
 
 def ipc_alloc(nbytes: int) -> tuple[int, bytes]:

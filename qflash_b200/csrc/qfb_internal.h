@@ -70,6 +70,14 @@ constexpr int kSigWords = kSigCount + 1;
 struct PeerSpec {
   int n;
   int8_t* o[kMaxPeers];
+  // Optional barrier inside the kernel (null sig: none): kSigWords uint32 per
+  // rank, zero-initialised, mapped like the copies; sig_peer in o's order;
+  // rank in [0, n]; epoch != 0, the same on every rank for one launch and
+  // growing from launch to launch.
+  uint32_t* sig;
+  uint32_t* sig_peer[kMaxPeers];
+  int rank;
+  uint32_t epoch;
 };
 int sm_count(int dev);
 

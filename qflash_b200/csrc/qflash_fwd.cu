@@ -263,7 +263,7 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, unsi
 // ------------------------------------------------------------------ kernel
 // SEGS = 2 packs two heads (of N <= 64 rows each) into one 128-row tile:
 // rows [0, 64) belong to head 2*item, rows [64, 128) to head 2*item + 1.
-template <int DQK, int DV, bool BIAS, int SEGS>
+template <int DQK, int DV, bool BIAS, int SEGS, bool GATHER = false>
 struct Cfg {
   static constexpr int SEG_ROWS = kBM / SEGS;
   static constexpr int QA = DQK < 128 ? DQK : 128;  // bytes per row of one swizzle atom
@@ -296,7 +296,7 @@ struct Cfg {
   static constexpr int OFF_V2 = OFF_V + KVS * V_BYTES;
   static constexpr int OFF_B = OFF_V2 + KVS * V2_BYTES;
   // int8 O rows of each softmax warp, staged for bulk copies (gathered output)
-  static constexpr int STG_BYTES = DV <= 64 ? 4 * 32 * DV : 0;
+  static constexpr int STG_BYTES = GATHER && DV <= 64 ? 4 * 32 * DV : 0;
   static constexpr int OFF_STG = OFF_B + KVS * B_BYTES;
   static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2;
@@ -333,12 +333,15 @@ __device__ __forceinline__ int swz_chunk(int r, int c, int w) { return c ^ (((r 
 // Flags other than DIV_FULL / DIV_IEEE must be 0 for every mode but kGen.
 enum Mode : int { kGen = 0, kFast = 1, kChecked = 2, kPlain = 3 };
 
-template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
-__global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__((Cfg<DQK, DV, BIAS, SEGS>::MAX_REGS))
+// GATHER compiles the gathered-output path (KArgs::n_peer, o_bulk, sig): the
+// copies into other GPUs' memory and the barrier over the ranks.
+template <int DQK, int DV, bool BIAS, int MODE, int SEGS, bool GATHER>
+__global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS, GATHER>::THREADS)
+    __maxnreg__((Cfg<DQK, DV, BIAS, SEGS, GATHER>::MAX_REGS))
     qfa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmB,
                    const KArgs a_in) {
-  using C = Cfg<DQK, DV, BIAS, SEGS>;
+  using C = Cfg<DQK, DV, BIAS, SEGS, GATHER>;
   // arguments are read in place (parameter space); the fixed-point constants
   // may come from the device parameter block instead
   const KArgs& a = a_in;
@@ -949,6 +952,14 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
             __all_sync(0xffffffffu, (l > 0 && l < (1 << 24) && (BIAS ? abound < 8388607.f : acc_bound(nch) < 8388607)) ||
                                         !row_ok);
         const float rcp = __frcp_ru(lf);
+        // gathered output: the warp's rows go through its staging rows in shared
+        // memory and leave as one bulk copy per destination
+        const bool bulk = GATHER && C::STG_BYTES > 0 && a.o_bulk;
+        const uint32_t stg = sbase + C::OFF_STG + warp * 32 * DV;
+        if (bulk) {
+          if (lane == 0) bulk_wait_read_all();  // the previous item's copies have read the staging rows
+          __syncwarp();
+        }
 #pragma unroll
         for (int part = 0; part < C::ACC_W / 32; ++part) {
           int v[32];
@@ -1006,6 +1017,11 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
                             ((long long)z * a.ou_z + (long long)h * a.ou_h + (long long)row * a.ou_n + a.v_col0 +
                              part * EPP) * esz;
             store_dequant<EPP>(drow, res, k_os, a.out_dtype, a.out_vec16);
+          } else if (row_ok && bulk) {
+#pragma unroll
+            for (int q4 = 0; q4 < EPP / 16; ++q4)
+              sts128(stg + lane * DV + part * EPP + 16 * q4,
+                     make_uint4(res[4 * q4], res[4 * q4 + 1], res[4 * q4 + 2], res[4 * q4 + 3]));
           } else if (row_ok) {
             int8_t* dst = orow + part * EPP;
             if (a.o_vec16) {
@@ -1014,25 +1030,43 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
                 const int4 val = make_int4((int)res[4 * q4], (int)res[4 * q4 + 1], (int)res[4 * q4 + 2],
                                            (int)res[4 * q4 + 3]);
                 *(int4*)(dst + 16 * q4) = val;
+                if (GATHER) {
 #pragma unroll 1
-                for (int pi = 0; pi < a.n_peer; ++pi) *(int4*)(dst + a.o_peer_off[pi] + 16 * q4) = val;
+                  for (int pi = 0; pi < a.n_peer; ++pi) *(int4*)(dst + a.o_peer_off[pi] + 16 * q4) = val;
+                }
               }
             } else {
 #pragma unroll
               for (int b = 0; b < EPP; ++b) dst[b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
 #pragma unroll 1
-              for (int pi = 0; pi < a.n_peer; ++pi)
+              for (int pi = 0; pi < (GATHER ? a.n_peer : 0); ++pi)
 #pragma unroll
                 for (int b = 0; b < EPP; ++b) dst[a.o_peer_off[pi] + b] = (int8_t)(res[b >> 2] >> (8 * (b & 3)));
             }
           }
         }
+        if (bulk) {
+          fence_proxy_async_smem();  // the staged rows are visible to the bulk copies
+          __syncwarp();
+          if (lane == 0) {
+            // the warp's rows [row0, row0 + nrows) are contiguous (row stride DV, checked on the host)
+            const uint32_t bytes = (uint32_t)min(32, a.N - row0) * DV;
+            int8_t* gdst = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row0 * a.os_n;
+            bulk_store(gdst, stg, bytes);
+#pragma unroll 1
+            for (int pi = 0; pi < a.n_peer; ++pi) bulk_store(gdst + a.o_peer_off[pi], stg, bytes);
+            bulk_commit();
+          }
+        }
       }
     }
-    // the peer copies' rows are performed system-wide before the kernel
-    // completes, so whatever follows it in stream order (the barrier
-    // collective) orders them before any reader on the other GPUs
-    if (a.n_peer > 0) __threadfence_system();
+    if (GATHER && C::STG_BYTES > 0 && a.o_bulk && lane == 0) {
+      bulk_wait_all();  // the bulk copies' global writes have completed
+      fence_proxy_async_global();
+    }
+    // the peer copies' rows are performed system-wide before this CTA reports
+    // itself finished (gather barrier below) or the kernel completes
+    if (GATHER && a.n_peer > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -1040,6 +1074,31 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS>::THREADS) __maxnreg__
   if (warp == 5) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (GATHER && a.sig && threadIdx.x == 0) {
+    // gather barrier (KArgs::sig): the last CTA to finish announces this rank's
+    // rows to every rank and waits, bounded, until every rank has announced
+    // this launch (flags only grow, so a rank already at the next launch counts)
+    __threadfence_system();
+    if (atomicAdd(a.sig + kSigCount, 1u) == gridDim.x - 1) {
+      a.sig[kSigCount] = 0;  // ready for the next launch
+      __threadfence_system();
+#pragma unroll 1
+      for (int pi = 0; pi < a.sig_world - 1; ++pi) st_release_sys(a.sig_peer[pi] + a.sig_rank, a.epoch);
+      st_release_sys(a.sig + a.sig_rank, a.epoch);
+      const long long t0 = clock64();
+#pragma unroll 1
+      for (int r = 0; r < a.sig_world; ++r) {
+        while ((int)(ld_acquire_sys(a.sig + r) - a.epoch) < 0) {
+          if (clock64() - t0 > kWaitCycles) {
+            atomicOr(&g_err, kErrPeer);
+            r = a.sig_world;
+            break;
+          }
+          __nanosleep(256);
+        }
+      }
+    }
   }
 }
 
@@ -1139,11 +1198,11 @@ int sm_count(int dev) {
   return n[dev];
 }
 
-template <int DQK, int DV, bool BIAS, int MODE, int SEGS>
+template <int DQK, int DV, bool BIAS, int MODE, int SEGS, bool GATHER>
 static int launch(int dev, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                   const CUtensorMap& mb, const KArgs& ka, cudaStream_t stream) {
-  using C = Cfg<DQK, DV, BIAS, SEGS>;
-  auto kern = qfa_fwd_kernel<DQK, DV, BIAS, MODE, SEGS>;
+  using C = Cfg<DQK, DV, BIAS, SEGS, GATHER>;
+  auto kern = qfa_fwd_kernel<DQK, DV, BIAS, MODE, SEGS, GATHER>;
   static int per_sm[kMaxDevices] = {0};
   static std::mutex mu;
   int ctas;
@@ -1319,6 +1378,23 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
       ka.o_peer_off[i] = (long long)((intptr_t)po - (intptr_t)o);
     }
     ka.n_peer = peers->n;
+    // a warp's 32 rows are one contiguous block when the rows are dense
+    ka.o_bulk = ka.o_vec16 && D <= 64 && o_strides[2] == D;
+  }
+  if (peers && peers->sig) {
+    if (fused_out) return set_err(QFLASH_ERR_UNSUPPORTED, "the gather barrier takes the int8 output only");
+    if (peers->rank < 0 || peers->rank > peers->n || peers->epoch == 0)
+      return set_err(QFLASH_ERR_ARG, "gather barrier: rank %d of %d, epoch %u", peers->rank, peers->n + 1,
+                     peers->epoch);
+    if ((uintptr_t)peers->sig & 3) return set_err(QFLASH_ERR_ALIGN, "signal words must be 4-byte aligned");
+    for (int i = 0; i < peers->n; ++i)
+      if (!peers->sig_peer[i] || ((uintptr_t)peers->sig_peer[i] & 3))
+        return set_err(QFLASH_ERR_ARG, "peer signal words %d are null or unaligned", i);
+    ka.sig = peers->sig;
+    for (int i = 0; i < peers->n; ++i) ka.sig_peer[i] = peers->sig_peer[i];
+    ka.sig_rank = peers->rank;
+    ka.sig_world = peers->n + 1;
+    ka.epoch = peers->epoch;
   }
   ka.rs = sm_rscale;
   ka.eM = exp_M;
@@ -1385,14 +1461,21 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
       return rc;
   }
   const int passes = D == 256 ? 2 : 1;
+  const bool gather = ka.n_peer > 0 || ka.sig;
+  uint32_t* const sig = ka.sig;
   for (int p = 0; p < passes; ++p) {
     ka.v_col0 = p * DV;
+    // the barrier closes the last pass only (a peer's flag then implies both of its passes)
+    ka.sig = p == passes - 1 ? sig : nullptr;
     // the compact default-arithmetic kernels unless a QFLASH_* form needs the general one
     const bool gen = flags & (QFLASH_FLAG_EXP_IDIV | QFLASH_FLAG_L_IDIV | QFLASH_FLAG_ACC_IDIV);
     const int mode = gen ? kGen : (bias ? kPlain : (ka.fast_exp == 1 ? kFast : (ka.fast_exp == 2 ? kChecked : kGen)));
+#define QFB_G(DQ, DVV, B, M, S)                                                   \
+  (gather ? launch<DQ, DVV, B, M, S, true>(dev, mq, mk, mv, mb, ka, stream)       \
+          : launch<DQ, DVV, B, M, S, false>(dev, mq, mk, mv, mb, ka, stream))
 #define QFB_LAUNCH(DQ, DVV, B, M) \
-  (segs == 2 ? launch<DQ, DVV, B, M, 2>(dev, mq, mk, mv, mb, ka, stream) : launch<DQ, DVV, B, M, 1>(dev, mq, mk, mv, mb, ka, stream))
-#define QFB_LAUNCH1(DQ, DVV, B, M) launch<DQ, DVV, B, M, 1>(dev, mq, mk, mv, mb, ka, stream)
+  (segs == 2 ? QFB_G(DQ, DVV, B, M, 2) : QFB_G(DQ, DVV, B, M, 1))
+#define QFB_LAUNCH1(DQ, DVV, B, M) QFB_G(DQ, DVV, B, M, 1)
 #define QFB_CASE(DQ, DVV, L)                                                      \
   if (bias)                                                                       \
     rc = mode == kGen ? L(DQ, DVV, true, kGen) : L(DQ, DVV, true, kPlain);        \
@@ -1408,6 +1491,7 @@ int attention_fwd(const int8_t* q, const int8_t* k, const int8_t* v, int8_t* o, 
       case 128: QFB_CASE(128, 128, QFB_LAUNCH1) break;
       default: QFB_CASE(256, 128, QFB_LAUNCH1) break;
     }
+#undef QFB_G
 #undef QFB_LAUNCH
 #undef QFB_LAUNCH1
 #undef QFB_CASE
@@ -1434,13 +1518,20 @@ extern "C" int qflash_i8_fwd_gather(const int8_t* q, const int8_t* k, const int8
                                     const int64_t bias_strides[4], int bias_z_period, int Z, int H, int N, int D,
                                     int32_t sm_rscale, int32_t exp_M, int32_t req_M, int64_t l_M, int64_t acc_M,
                                     int32_t l_shift, int32_t acc_shift, uint32_t flags, int8_t* const* o_peers,
-                                    int n_peers, void* stream) {
+                                    int n_peers, uint32_t* sig, uint32_t* const* sig_peers, int rank,
+                                    uint32_t epoch, void* stream) {
   if (n_peers < 0 || n_peers > qfb::kMaxPeers || (n_peers > 0 && !o_peers))
     return qfb::set_err(QFLASH_ERR_ARG, "n_peers %d (0..%d, with a pointer array)", n_peers, qfb::kMaxPeers);
+  if (sig && n_peers > 0 && !sig_peers) return qfb::set_err(QFLASH_ERR_ARG, "signal words without the peers'");
   qfb::PeerSpec ps;
   memset(&ps, 0, sizeof(ps));
   ps.n = n_peers;
   for (int i = 0; i < n_peers; ++i) ps.o[i] = o_peers[i];
+  ps.sig = sig;
+  if (sig)
+    for (int i = 0; i < n_peers; ++i) ps.sig_peer[i] = sig_peers[i];
+  ps.rank = rank;
+  ps.epoch = epoch;
   return qfb::attention_fwd(q, k, v, o, bias, q_strides, k_strides, v_strides, o_strides, bias_strides,
                             bias_z_period, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M, l_shift, acc_shift, flags,
                             nullptr, nullptr, stream, &ps);
@@ -1493,6 +1584,84 @@ extern "C" int qflash_selftest_wait_timeout(void* stream, long long max_cycles) 
   qfb::wait_selftest_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(max_cycles);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "selftest launch: %s", cudaGetErrorString(e));
+  return QFLASH_OK;
+}
+
+namespace qfb {
+// Max-reduction of up to 4 floats over the ranks through their signal words
+// (qflash_peer_max).  Word layout after the gather barrier's: flags at
+// kXFlag + r, values at kXVal + 4 * (8 * (epoch & 1) + r) -- two buffers by
+// epoch parity, so a rank already at the next exchange writes the other one.
+constexpr int kXFlag = 16, kXVal = 64;
+struct PeerMaxArgs {
+  const float* in;
+  float* out;
+  uint32_t* sig;
+  uint32_t* sig_peer[kMaxPeers];
+  int n, rank, world;
+  uint32_t epoch;
+};
+
+// max that keeps a NaN (torch's amax propagates it)
+__device__ __forceinline__ float max_nan(float a, float b) { return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b); }
+
+__global__ void peer_max_kernel(const __grid_constant__ PeerMaxArgs a) {
+  const int par = 8 * (a.epoch & 1);
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = i < a.n ? a.in[i] : 0.f;
+  for (int p = 0; p < a.world; ++p) {
+    uint32_t* w = p == a.world - 1 ? a.sig : a.sig_peer[p];
+    volatile float* slot = (volatile float*)(w + kXVal + 4 * (par + a.rank));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) slot[i] = v[i];
+  }
+  __threadfence_system();
+  for (int p = 0; p < a.world; ++p) st_release_sys((p == a.world - 1 ? a.sig : a.sig_peer[p]) + kXFlag + a.rank, a.epoch);
+  const long long t0 = clock64();
+  for (int r = 0; r < a.world; ++r) {
+    while ((int)(ld_acquire_sys(a.sig + kXFlag + r) - a.epoch) < 0) {
+      if (clock64() - t0 > kWaitCycles) {
+        atomicOr(&g_err, kErrPeer);
+        for (int i = 0; i < a.n; ++i) a.out[i] = __int_as_float(0x7fc00000);
+        return;
+      }
+      __nanosleep(128);
+    }
+  }
+  for (int i = 0; i < a.n; ++i) {
+    float m = ((volatile float*)(a.sig + kXVal + 4 * par))[i];
+    for (int r = 1; r < a.world; ++r) m = max_nan(m, ((volatile float*)(a.sig + kXVal + 4 * (par + r)))[i]);
+    a.out[i] = m;
+  }
+}
+}  // namespace qfb
+
+extern "C" int qflash_peer_max(const float* in, int n, float* out, uint32_t* sig, uint32_t* const* sig_peers,
+                               int n_peers, int rank, uint32_t epoch, void* stream) {
+  if (!in || !out || !sig || n < 1 || n > 4 || n_peers < 0 || n_peers > qfb::kMaxPeers || rank < 0 ||
+      rank > n_peers || epoch == 0 || (n_peers > 0 && !sig_peers) || ((uintptr_t)sig & 15))
+    return set_err(QFLASH_ERR_ARG, "peer_max: n %d, n_peers %d, rank %d, epoch %u", n, n_peers, rank, epoch);
+  qfb::PeerMaxArgs pa;
+  memset(&pa, 0, sizeof(pa));
+  pa.in = in;
+  pa.out = out;
+  pa.sig = sig;
+  for (int i = 0; i < n_peers; ++i) {
+    if (!sig_peers[i] || ((uintptr_t)sig_peers[i] & 15))
+      return set_err(QFLASH_ERR_ARG, "peer signal words %d are null or unaligned", i);
+    pa.sig_peer[i] = sig_peers[i];
+  }
+  pa.n = n;
+  pa.rank = rank;
+  pa.world = n_peers + 1;
+  pa.epoch = epoch;
+  DeviceGuard keep_device;
+  int dev = 0;
+  if (int rc = select_device(sig, &dev)) return rc;
+  qfb::peer_max_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(pa);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "peer_max launch: %s", cudaGetErrorString(e));
   return QFLASH_OK;
 }
 

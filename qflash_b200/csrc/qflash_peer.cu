@@ -18,6 +18,11 @@ extern "C" int qflash_ipc_alloc(size_t bytes, void** ptr, void* handle) {
   void* p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess)
     return qfb::set_err(QFLASH_ERR_DEVICE, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(cudaGetLastError()));
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {  // signal words start at 0
+    const cudaError_t e = cudaGetLastError();
+    cudaFree(p);
+    return qfb::set_err(QFLASH_ERR_DEVICE, "cudaMemset: %s", cudaGetErrorString(e));
+  }
   cudaIpcMemHandle_t h;
   if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
     const cudaError_t e = cudaGetLastError();

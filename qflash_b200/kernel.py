@@ -152,11 +152,13 @@ def do_bench(fn, warmup: float = 10, rep: float = 100) -> float:
 def launch_int8(q8: Tensor, k8: Tensor, v8: Tensor, o8: Tensor, sm_rscale: int, exp_M: int, req_M: int,
                 l_M: int, acc_M: int, bias: Tensor | None = None, bias_strides=None,
                 l_shift: int = None, acc_shift: int = None, flags: int = None, stream=None,
-                bias_z_period: int = 0, o_peers=None) -> None:
+                bias_z_period: int = 0, o_peers=None, barrier=None) -> None:
     """Run the sm_100a kernel on int8 [Z, H, N, D] tensors already on the GPU
     (the launch at qflash/kernel.py:319-326 / 339-346).  ``o_peers``: addresses
     of o8's rows in other GPUs' copies of a gathered output (``shard.PeerOutput``),
-    which the epilogue fills as well."""
+    which the epilogue fills as well; ``barrier``: the gather barrier's
+    (sig, sig_peers, rank, epoch), after which the kernel completes only once
+    every rank's rows are in every copy."""
     for t in (q8, k8, v8, o8):
         if not t.is_cuda or t.dtype != torch.int8 or t.dim() != 4:
             raise ValueError("q, k, v, o must be 4-D int8 CUDA tensors")
@@ -168,7 +170,7 @@ def launch_int8(q8: Tensor, k8: Tensor, v8: Tensor, o8: Tensor, sm_rscale: int, 
             raise OverflowError(f"{name}={val} does not fit in int32")
     _lib.i8_fwd(q8, k8, v8, o8, bias, bias_strides, Z, H, N, D, sm_rscale, exp_M, req_M, l_M, acc_M,
                 L_SHIFT if l_shift is None else l_shift, ACC_SHIFT if acc_shift is None else acc_shift,
-                arith_flags() if flags is None else flags, stream, bias_z_period, o_peers)
+                arith_flags() if flags is None else flags, stream, bias_z_period, o_peers, barrier)
 
 
 def qflash_forward(
@@ -297,7 +299,7 @@ def tensor_scales(query: Tensor, key: Tensor, value: Tensor):
 
 def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mode='output',
                         scales=None, launch=None, return_int8=False, bias_z_period=0,
-                        o_out=None, o_peers=None, dequant=True):
+                        o_out=None, o_peers=None, dequant=True, barrier=None):
     """The body of ``qflash.forward`` with seams: ``scales`` supplies
     (q_scale, k_scale, o_scale) computed elsewhere (the sharded path reduces
     them over all ranks so each shard quantises exactly like the whole
@@ -306,8 +308,9 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
     ``attn_mask`` has that many batch entries and batch z uses entry
     z % bias_z_period (see ``window_attention``).  ``o_out`` is the int8 output
     tensor to write (default: a new one), ``o_peers`` the addresses of its rows
-    in other GPUs' copies (``shard.PeerOutput``), and ``dequant=False`` skips
-    the local ``o * o_scale`` (returned as None)."""
+    in other GPUs' copies (``shard.PeerOutput``), ``barrier`` the gather
+    barrier of that launch, and ``dequant=False`` skips the local
+    ``o * o_scale`` (returned as None)."""
     HEAD_DIM_Q, HEAD_DIM_K = query.shape[-1], key.shape[-1]
     HEAD_DIM_V = value.shape[-1]
     assert HEAD_DIM_Q == HEAD_DIM_K and HEAD_DIM_K == HEAD_DIM_V
@@ -344,7 +347,7 @@ def forward_with_scales(query, key, value, attn_mask=None, scale=None, return_mo
             launch(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides)
         else:
             launch_int8(query, key, value, o, sm_rscale, exp_M, req_M, l_M, acc_M, bias, bias_strides,
-                        bias_z_period=bias_z_period, o_peers=o_peers)
+                        bias_z_period=bias_z_period, o_peers=o_peers, barrier=barrier)
 
     if return_mode == 'latency':
         return do_bench(kernel, warmup=10, rep=100)

@@ -9,9 +9,10 @@ scalars before quantising -- after that every shard's int8 values and
 fixed-point constants are bit-identical to what a single process computes on
 the full tensor.  ``gather=True`` collects the int8 outputs on every rank:
 with a ``PeerOutput`` the attention epilogue itself stores every row into
-every rank's copy of the gathered output over NVLink (one small all_reduce
-afterwards orders those stores before any rank reads), otherwise NCCL
-all_gather runs after the kernel; nothing else crosses GPUs.
+every rank's copy of the gathered output over NVLink, and the kernel ends with
+a barrier over the ranks (flags written into the peers' signal words, so the
+kernel completes only once every copy is whole); otherwise NCCL all_gather
+runs after the kernel.  Nothing else crosses GPUs.
 """
 from __future__ import annotations
 
@@ -24,6 +25,7 @@ from . import _lib
 from .kernel import forward_with_scales, tensor_scales
 
 MAX_RANKS = 8   # the epilogue stores into at most 7 peer copies
+SIG_BYTES = 4 * _lib.SIG_WORDS  # signal words of the gather barrier and of the scale exchange
 
 
 def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -35,15 +37,18 @@ def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
-def global_scales(query, key, value, group=None):
+def global_scales(query, key, value, group=None, peer=None):
     """(q_scale, k_scale, o_scale) of the full tensors from this rank's shards.
 
     amax is exact under max-reduction; the values travel as fp32 (exact for
     fp16/bf16/fp32 inputs) and the division by 127 happens afterwards in the
-    input dtype, as in the single-process path."""
+    input dtype, as in the single-process path.  With ``peer`` (a PeerOutput)
+    the maxima are exchanged through its signal words, else all_reduce."""
     dt = query.dtype
     local = torch.stack([t.abs().amax().to(torch.float32) for t in (query, key, value)])
-    if dist.is_available() and dist.is_initialized():
+    if peer is not None:
+        local = peer.max_(local)
+    elif dist.is_available() and dist.is_initialized():
         dist.all_reduce(local, op=dist.ReduceOp.MAX, group=group)
     i8max = torch.iinfo(torch.int8).max
     return tuple(local[i].to(dt) / i8max for i in range(3))
@@ -79,7 +84,11 @@ class PeerOutput:
         if len(self.shape) != 4:
             raise ValueError("PeerOutput holds a [Z, H, N, D] tensor")
         self.device = torch.device("cuda", torch.cuda.current_device())
-        self._ptr, handle = _lib.ipc_alloc(max(1, math.prod(self.shape)))
+        # the int8 copy, then (256-byte aligned) the gather barrier's signal words
+        self._sig_off = -(-math.prod(self.shape) // 256) * 256
+        self._ptr, handle = _lib.ipc_alloc(self._sig_off + SIG_BYTES)
+        self._epoch = 0
+        self._max_epoch = 0
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group)
         self._peers = [_lib.ipc_open(h) for r, h in enumerate(handles) if r != self.rank]
@@ -91,6 +100,25 @@ class PeerOutput:
         """Addresses of batch entry z0 in every other rank's copy."""
         row = math.prod(self.shape[1:])
         return [p + z0 * row for p in self._peers]
+
+    def next_barrier(self):
+        """(sig, sig_peers, rank, epoch) for the next launch: every rank calls
+        this once per launch, so the epochs agree."""
+        self._epoch = self._epoch % 0x7fffffff + 1
+        return (self._ptr + self._sig_off, [p + self._sig_off for p in self._peers], self.rank, self._epoch)
+
+    def max_(self, values: torch.Tensor) -> torch.Tensor:
+        """Max over the ranks of up to 4 float32 values on this rank's device
+        (qflash_peer_max: written into every rank's signal words over NVLink,
+        no library collective); NaN wins.  Collective: every rank calls it."""
+        if values.dtype != torch.float32 or values.numel() > 4 or not values.is_cuda:
+            raise ValueError("up to 4 float32 CUDA values")
+        self._max_epoch = self._max_epoch % 0x7fffffff + 1
+        inp = values.contiguous()
+        out = torch.empty_like(inp)
+        _lib.peer_max(inp, out, self._ptr + self._sig_off, [p + self._sig_off for p in self._peers], self.rank,
+                      self._max_epoch, torch.cuda.current_stream(self.device).cuda_stream)
+        return out
 
     def close(self):
         """Unmap the peers' copies and free this one (collective)."""
@@ -116,7 +144,7 @@ def forward_sharded(query, key, value, attn_mask=None, scale=None, group=None, g
     from every rank's int8 shard -- written by the attention epilogue into
     ``peer_out`` on every rank when given (shards in rank order), else
     collected with NCCL all_gather."""
-    scales = global_scales(query, key, value, group)
+    scales = global_scales(query, key, value, group, peer_out if gather else None)
     world = dist.get_world_size(group)
     if gather and peer_out is not None:
         sizes = torch.tensor([query.shape[0]], device=query.device)
@@ -129,12 +157,10 @@ def forward_sharded(query, key, value, attn_mask=None, scale=None, group=None, g
             raise ValueError(f"peer_out holds {peer_out.shape}, the shards make "
                              f"{(sum(all_sizes),) + tuple(query.shape[1:])}")
         o_local = peer_out.buffer[z0:z0 + query.shape[0]]
+        # the kernel completes only once every rank's rows are in every copy
         _, _, o_scale = forward_with_scales(query, key, value, attn_mask, scale, scales=scales, launch=launch,
                                             return_int8=True, o_out=o_local, o_peers=peer_out.peer_rows(z0),
-                                            dequant=False)
-        # every rank's kernel precedes its part of this collective in stream
-        # order, so after it all peer stores into this rank's copy are done
-        dist.all_reduce(torch.zeros(1, device=query.device), group=group)
+                                            dequant=False, barrier=peer_out.next_barrier())
         return peer_out.buffer * o_scale
     out, o8, o_scale = forward_with_scales(query, key, value, attn_mask, scale, scales=scales,
                                            launch=launch, return_int8=True)

@@ -37,6 +37,8 @@ def _worker(rank, world, port, path, fused):
         outs.append(forward_sharded(q[a:b].contiguous(), k[a:b].contiguous(), v[a:b].contiguous(), gather=True,
                                     peer_out=peer).cpu())
     torch.cuda.synchronize()
+    from qflash_b200 import _lib
+    assert _lib.device_error(torch.cuda.current_stream().cuda_stream) == 0
     torch.save(outs, os.path.join(path, f"r{rank}.pt"))
     if peer is not None:
         peer.close()
