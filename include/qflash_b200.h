@@ -128,7 +128,7 @@ int qflash_i8_fwd_gather(const int8_t* q, const int8_t* k, const int8_t* v, int8
  * bounded (~2 s; a timeout sets bit 256 of the device error word and writes
  * NaN), for all flags of this epoch.  NaN wins, as in torch's amax.  Used for
  * the global quantisation scales of a sharded forward (one launch of one
- * thread instead of a library all_reduce).  epoch as for the gather barrier,
+ * warp instead of a library all_reduce).  epoch as for the gather barrier,
  * counted separately from it.
  */
 int qflash_peer_max(const float* in, int n, float* out, uint32_t* sig, uint32_t* const* sig_peers, int n_peers,

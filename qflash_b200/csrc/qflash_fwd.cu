@@ -1053,8 +1053,13 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS, GATHER>::THREADS)
             const uint32_t bytes = (uint32_t)min(32, a.N - row0) * DV;
             int8_t* gdst = a.o + (long long)z * a.os_z + (long long)h * a.os_h + (long long)row0 * a.os_n;
             bulk_store(gdst, stg, bytes);
+            // the peers in an order that differs by CTA and warp, so that the
+            // GPU's copies spread over every destination instead of all SMs
+            // (of every rank) writing to the same peer at once
+            int pi = (int)((blockIdx.x * 4u + (unsigned)warp) % (unsigned)a.n_peer);
 #pragma unroll 1
-            for (int pi = 0; pi < a.n_peer; ++pi) bulk_store(gdst + a.o_peer_off[pi], stg, bytes);
+            for (int c = 0; c < a.n_peer; ++c, pi = pi + 1 == a.n_peer ? 0 : pi + 1)
+              bulk_store(gdst + a.o_peer_off[pi], stg, bytes);
             bulk_commit();
           }
         }
@@ -1606,33 +1611,39 @@ struct PeerMaxArgs {
 __device__ __forceinline__ float max_nan(float a, float b) { return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b); }
 
 __global__ void peer_max_kernel(const __grid_constant__ PeerMaxArgs a) {
+  // thread p < world serves rank p (p == world - 1: this rank's own words):
+  // it writes this rank's values and flag there, then waits for rank p's flag
+  // here, so the remote stores and the waits run side by side
+  __shared__ int failed;
   const int par = 8 * (a.epoch & 1);
-  float v[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] = i < a.n ? a.in[i] : 0.f;
-  for (int p = 0; p < a.world; ++p) {
+  const int p = threadIdx.x;
+  if (p == 0) failed = 0;
+  __syncthreads();
+  if (p < a.world) {
     uint32_t* w = p == a.world - 1 ? a.sig : a.sig_peer[p];
     volatile float* slot = (volatile float*)(w + kXVal + 4 * (par + a.rank));
 #pragma unroll
-    for (int i = 0; i < 4; ++i) slot[i] = v[i];
-  }
-  __threadfence_system();
-  for (int p = 0; p < a.world; ++p) st_release_sys((p == a.world - 1 ? a.sig : a.sig_peer[p]) + kXFlag + a.rank, a.epoch);
-  const long long t0 = clock64();
-  for (int r = 0; r < a.world; ++r) {
-    while ((int)(ld_acquire_sys(a.sig + kXFlag + r) - a.epoch) < 0) {
+    for (int i = 0; i < 4; ++i) slot[i] = i < a.n ? a.in[i] : 0.f;
+    __threadfence_system();
+    st_release_sys(w + kXFlag + a.rank, a.epoch);
+    const long long t0 = clock64();
+    while ((int)(ld_acquire_sys(a.sig + kXFlag + p) - a.epoch) < 0) {
       if (clock64() - t0 > kWaitCycles) {
         atomicOr(&g_err, kErrPeer);
-        for (int i = 0; i < a.n; ++i) a.out[i] = __int_as_float(0x7fc00000);
-        return;
+        failed = 1;
+        break;
       }
-      __nanosleep(128);
+      __nanosleep(64);
     }
   }
-  for (int i = 0; i < a.n; ++i) {
-    float m = ((volatile float*)(a.sig + kXVal + 4 * par))[i];
-    for (int r = 1; r < a.world; ++r) m = max_nan(m, ((volatile float*)(a.sig + kXVal + 4 * (par + r)))[i]);
-    a.out[i] = m;
+  __syncthreads();
+  if (p < a.n) {
+    float m = __int_as_float(0x7fc00000);
+    if (!failed) {
+      m = ((volatile float*)(a.sig + kXVal + 4 * par))[p];
+      for (int r = 1; r < a.world; ++r) m = max_nan(m, ((volatile float*)(a.sig + kXVal + 4 * (par + r)))[p]);
+    }
+    a.out[p] = m;
   }
 }
 }  // namespace qfb
@@ -1659,7 +1670,7 @@ extern "C" int qflash_peer_max(const float* in, int n, float* out, uint32_t* sig
   DeviceGuard keep_device;
   int dev = 0;
   if (int rc = select_device(sig, &dev)) return rc;
-  qfb::peer_max_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(pa);
+  qfb::peer_max_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(pa);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_err(QFLASH_ERR_LAUNCH, "peer_max launch: %s", cudaGetErrorString(e));
   return QFLASH_OK;
