@@ -207,6 +207,9 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
+        # no NVLink multicast objects in this job (NCCL's NVLS algorithms bind
+        # them; the library's own collectives use plain peer stores)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     from qflash_b200 import _lib
     from qflash_b200 import kernel as K
