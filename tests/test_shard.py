@@ -126,3 +126,82 @@ def test_peer_output_needs_a_process_group():
         pytest.skip("a process group is already initialised")
     with pytest.raises(RuntimeError, match="process group"):
         PeerOutput((2, 3, 40, 32))
+
+
+class _FakePeerOutput:
+    """Stands in for shard.PeerOutput on CPU: the gathered copy is a plain
+    tensor, the scale exchange a gloo all_reduce, and the launch stub below
+    plays the epilogue's peer stores with an all_gather."""
+
+    def __init__(self, shape):
+        self.shape = tuple(shape)
+        self.buffer = torch.full(self.shape, 99, dtype=torch.int8)
+        self.epochs = []
+
+    def peer_rows(self, z0):
+        return [z0]
+
+    def next_barrier(self):
+        self.epochs.append(len(self.epochs) + 1)
+        return (0, [], dist.get_rank(), self.epochs[-1])
+
+    def max_(self, values):
+        out = values.clone()
+        dist.all_reduce(out, op=dist.ReduceOp.MAX)
+        return out
+
+
+def _peer_stub(peer, sizes):
+    def launch(q8, k8, v8, o8, rs, eM, rM, lM, aM, bias=None, bs=None):
+        z0 = sum(sizes[:dist.get_rank()])              # this rank's rows sit at its batch offset
+        assert o8.data_ptr() == peer.buffer[z0].data_ptr() and o8.shape[0] == sizes[dist.get_rank()]
+        o8.copy_(v8)                                   # the local rows, written into the gathered copy
+        zmax = max(sizes)                              # every other rank's rows, as its epilogue stores them
+        mine = torch.zeros((zmax,) + tuple(o8.shape[1:]), dtype=torch.int8)
+        mine[:o8.shape[0]] = o8
+        parts = [torch.zeros_like(mine) for _ in sizes]
+        dist.all_gather(parts, mine)
+        peer.buffer.copy_(torch.cat([p[:n] for p, n in zip(parts, sizes)]))
+    return launch
+
+
+def _peer_worker(rank, world, port, path, Z):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(Z, 3, 40, 32, generator=g) for _ in range(3))
+    a, b = shard_bounds(Z, world, rank)
+    sizes = [e - s for s, e in (shard_bounds(Z, world, r) for r in range(world))]
+    peer = _FakePeerOutput(q.shape)
+    outs = [forward_sharded(q[a:b], k[a:b], v[a:b], gather=True, launch=_peer_stub(peer, sizes), peer_out=peer)
+            for _ in range(2)]
+    bad = None
+    try:
+        forward_sharded(q[a:b], k[a:b], v[a:b], gather=True, launch=_peer_stub(peer, sizes),
+                        peer_out=_FakePeerOutput((Z + 1,) + tuple(q.shape[1:])))
+    except ValueError as e:
+        bad = str(e)
+    torch.save({"outs": outs, "epochs": peer.epochs, "bad": bad}, os.path.join(path, f"r{rank}.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("Z", [4, 5])
+def test_sharded_forward_with_peer_output_host_logic(Z):
+    """forward_sharded(gather=True, peer_out=...): global scales through the
+    peer exchange, this rank's rows at its batch offset of the gathered copy,
+    one barrier epoch per call, the dequantised whole output on every rank,
+    and a copy of the wrong shape rejected."""
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_peer_worker, args=(world, _free_port(), d, Z), nprocs=world, start_method="spawn",
+                           join=True)
+        res = [torch.load(os.path.join(d, f"r{r}.pt")) for r in range(world)]
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(Z, 3, 40, 32, generator=g) for _ in range(3))
+    full = K.forward_with_scales(q, k, v, launch=_stub({}))
+    for r in res:
+        assert r["epochs"] == [1, 2]
+        for o in r["outs"]:
+            assert torch.equal(o, full)
+        assert r["bad"] is not None and "peer_out holds" in r["bad"]
