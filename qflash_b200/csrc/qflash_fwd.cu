@@ -296,7 +296,7 @@ struct Cfg {
   static constexpr int OFF_V2 = OFF_V + KVS * V_BYTES;
   static constexpr int OFF_B = OFF_V2 + KVS * V2_BYTES;
   // int8 O rows of each softmax warp, staged for bulk copies (gathered output)
-  static constexpr int STG_BYTES = GATHER && DV <= 64 ? 4 * 32 * DV : 0;
+  static constexpr int STG_BYTES = GATHER && DV <= 64 ? 2 * 4 * 32 * DV : 0;  // two buffers per warp
   static constexpr int OFF_STG = OFF_B + KVS * B_BYTES;
   static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int NBAR = 2 + 2 + KVS + KVS + 2 + 2 + 2;
@@ -628,6 +628,7 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS, GATHER>::THREADS)
     const bool lb_launch = !BIAS && !GEN && s_pair && S >= 10 && nch_launch_ok &&
                            (long long)rs * k_accM - (1ll << S) <= (1ll << (S - 10));
     uint32_t g = 0;
+    int stg_buf = 0;  // staging buffer of the next gathered-output epilogue
     bool ok = true;
     for (int k = 0, item = item_of(0); ok && item >= 0; item = item_of(++k)) {
       // warp -> segment (head) and its 32-row slice
@@ -958,10 +959,13 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS, GATHER>::THREADS)
         // gathered output: the warp's rows go through its staging rows in shared
         // memory and leave as one bulk copy per destination
         const bool bulk = GATHER && C::STG_BYTES > 0 && a.o_bulk;
-        const uint32_t stg = sbase + C::OFF_STG + warp * 32 * DV;
+        // two staging buffers per warp, alternating by item: the copies of the
+        // previous item may still be reading the other one
+        const uint32_t stg = sbase + C::OFF_STG + (stg_buf * 4 + warp) * 32 * DV;
         if (bulk) {
-          if (lane == 0) bulk_wait_read_all();  // the previous item's copies have read the staging rows
+          if (lane == 0) bulk_wait_read_but_last();  // the copies of two items ago have read this buffer
           __syncwarp();
+          stg_buf ^= 1;
         }
 #pragma unroll
         for (int part = 0; part < C::ACC_W / 32; ++part) {

@@ -70,8 +70,11 @@ __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t b
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// every bulk group this thread committed has finished reading shared memory
-__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// all but the most recent bulk group this thread committed have finished
+// reading shared memory
+__device__ __forceinline__ void bulk_wait_read_but_last() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // every bulk group this thread committed has completed its global writes
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
