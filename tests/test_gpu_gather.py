@@ -27,11 +27,13 @@ def _launch(q8, k8, v8, o, prm, o_peers, barrier):
     K.launch_int8(q8, k8, v8, o, *prm, o_peers=o_peers, barrier=barrier)
 
 
-@pytest.mark.parametrize("Z,H,N,D", [(3, 4, 197, 64), (2, 3, 49, 32), (2, 2, 100, 128), (1, 1, 5, 64)])
+@pytest.mark.parametrize("Z,H,N,D", [(3, 4, 197, 64), (2, 3, 49, 32), (2, 2, 100, 128), (1, 1, 5, 64),
+                                     (2, 2, 70, 256)])
 def test_gather_copies_equal_local_output(Z, H, N, D):
     """Every row lands in o and in each peer copy, for the bulk-copy layouts
-    (dense rows, D <= 64) and the per-thread stores (D = 128); the barrier
-    passes when every rank's flag is set."""
+    (dense rows, D <= 64) and the per-thread stores (D = 128, and D = 256,
+    which runs as two launches with the barrier closing the second); the
+    barrier passes when every rank's flag is set."""
     from qflash_b200 import _lib
     from qflash_b200 import kernel as K
     (q8, k8, v8), prm = _case(Z, H, N, D)
