@@ -365,6 +365,10 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS, GATHER>::THREADS)
     k_mlim = (int)dp[6];
     k_os = __int_as_float((int)dp[P_OS]);
   }
+  // kChecked (no bias): every score is an int8 dot product, |s| < DQK * 2^14,
+  // so when m_lim is at least that the 6-op exp2 holds for every chunk and the
+  // per-chunk vote is not needed
+  const bool k_fast_all = MODE == kChecked && k_mlim >= (DQK << 14);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
@@ -790,7 +794,7 @@ __global__ void __launch_bounds__(Cfg<DQK, DV, BIAS, SEGS, GATHER>::THREADS)
                                    __vimax3_s32(t3[6], t3[7], t3[8])),
                       __vimax3_s32(t3[9], t3[10], m));
           bool use_fast = MODE == kFast;
-          if (MODE == kChecked) use_fast = __all_sync(0xffffffffu, m_new < k_mlim);
+          if (MODE == kChecked) use_fast = k_fast_all || __all_sync(0xffffffffu, m_new < k_mlim);
           // In a ragged last chunk every padded column holds NEG_INF, so all of
           // them share one P value: groups of four columns past the last valid
           // one (whole eighths of the chunk) take it without recomputation.
